@@ -1,0 +1,290 @@
+"""Verified tokens/s of the Qwen3.5-27B-shape 4-bit decode / K-token verify step.
+
+Workload: the full 64-layer stack (48 GatedDeltaNet + 16 attention layers,
+MLX affine 4-bit weights, bf16 embedding, 4-bit lm_head), random-init
+synthetic weights generated on the GPU, seeded recurrent state and a KV cache
+of 1024 prior tokens; each step verifies K = 32 draft tokens (the headline)
+and, reported alongside, K = 1 (plain decode).  One step = one pass of the
+whole stack over the K tokens + lm_head argmax + accept length; positions
+advance by K every step (context 1024 -> 1024 + (W+S)*K).
+
+  python bench.py [--gpus N] [--steps S] [--warmup W] [--k 32] [--impl reference]
+
+With N > 1 (one process per GPU under torch.distributed.run) the step runs
+tensor-parallel over N GPUs (NCCL all-reduce of the row-parallel outputs), so
+the total work is fixed and scaling is strong.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "inference-across-metal_b200"))
+
+SEED = 20261201
+CTX = 1024
+METRIC = "verified tokens/sec, Qwen3.5-27B-shape 4-bit at K=1/32, and % of HBM roofline"
+WORKLOAD = "qwen3.5-27b-shape 64-layer (48 GDN + 16 attn) 4-bit verify, ctx 1024, batch 1"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        def run():
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.samples.append([x.strip() for x in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- CPU legs (oracle)
+def oracle_sample(K: int, threads: int):
+    """Time the CPU restatement (numpy fp32, dequant included) on one GDN layer,
+    one attention layer and 1/16 of the lm_head at full size; extrapolate to
+    the 64-layer step.  Returns (tokens/s, seconds of CPU work, description)."""
+    import numpy as np
+    from oracle import iam_oracle as O
+    from oracle import synth_model as SM
+    d = O.QWEN35_27B
+    W = SM.make_layer(SEED, d, 0)
+    W.update(SM.make_layer(SEED, d, 3))
+    st = SM.make_state(SEED, d, CTX, CTX + K, layers=[0, 3])
+    lm_rows = d.vocab // 16
+    w, s, b = SM.make_tensor(SEED, "lm_head", "q4", (lm_rows, d.hidden), None)
+    x = SM.hidden_input(SEED, d, K)
+    t0 = time.perf_counter()
+    O.gdn_block(x, W, "model.layers.0.", st.conv[0], st.S[0], d)
+    t1 = time.perf_counter()
+    O.attn_block(x, W, "model.layers.3.", st.k_cache[3], st.v_cache[3], CTX, d)
+    t2 = time.perf_counter()
+    O.argmax_first(O.qmm_affine4(O.rms_norm(x, np.ones(d.hidden, np.float32)), w, s, b))
+    t3 = time.perf_counter()
+    step = 48 * (t1 - t0) + 16 * (t2 - t1) + 16 * (t3 - t2)
+    desc = (f"numpy fp32 oracle, {threads} threads: 1 GDN layer {t1 - t0:.2f}s + 1 attention layer {t2 - t1:.2f}s "
+            f"+ 1/16 lm_head {t3 - t2:.2f}s at K={K}, ctx {CTX}, extrapolated x48/x16/x16 to the 64-layer step")
+    return K / step, t3 - t0, desc
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, _, desc = oracle_sample(args.k, threads)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * args.k / value,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "K": args.k, "ctx": CTX, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU
+def run_gpu(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import iam_b200 as I
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    K = args.k
+    ksteps = args.warmup + args.steps
+    max_ctx = CTX + (ksteps + 2) * max(K, 1) * 2 + 64
+    dims = I.Dims.qwen35_27b(max_ctx=max_ctx, max_rows=max(32, K))
+    nccl_id = None
+    if world > 1:
+        obj = [I.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    eng = I.Engine(dims, device=local_rank, rank=rank, world=world, nccl_id=nccl_id)
+    eng.init_synthetic(SEED)
+    rng = np.random.default_rng(SEED)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def device_run(kk: int):
+        eng.state_init(SEED, CTX)
+        toks = torch.from_numpy(rng.integers(0, dims.vocab, kk).astype(np.int32)).cuda()
+        out = torch.zeros(kk, dtype=torch.int32, device="cuda")
+        eng.verify_device(toks.data_ptr(), kk, CTX, out.data_ptr(), sh)
+        for _ in range(args.warmup - 1):
+            eng.verify_device(toks.data_ptr(), kk, -1, out.data_ptr(), sh)
+        barrier()
+        clk = ClockSampler(local_rank)
+        clk.start()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            eng.verify_device(toks.data_ptr(), kk, -1, out.data_ptr(), sh)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        clocks = clk.stop()
+        if dist is not None:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        barrier()
+        return ms, clocks
+
+    ms32, clocks = device_run(K)
+    ms1, _ = device_run(1) if K != 1 else (ms32, None)
+
+    # end to end through the public C API: host tokens in, host argmax out
+    eng.state_init(SEED, CTX)
+    htoks = rng.integers(0, dims.vocab, K).astype(np.int32)
+    pos = CTX
+    for _ in range(args.warmup):
+        eng.verify(htoks, pos)
+        pos += K
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.verify(htoks, pos)
+        pos += K
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if dist is not None:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    # per-kernel-kind device time of one eager step (CUDA events on the engine stream)
+    eng.state_init(SEED, CTX)
+    prof = eng.profile_step(K, CTX)
+    launches = eng.step_launches(K)
+    step_bytes = eng.step_bytes(K, CTX)
+    hbm, peak_kind = peaks()
+    q = prof.get("qmm", {"ms": 0.0, "bytes": 0.0, "launches": 1})
+    q_gbs = q["bytes"] / (q["ms"] / 1000.0) / 1e9 if q["ms"] > 0 else 0.0
+    eng.close()
+
+    if rank != 0:
+        return
+    step_gbs = step_bytes / (ms32 / 1000.0) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": K * 1000.0 / ms32,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms32,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "K": K, "ctx": CTX, "batch": 1, "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2 (14.4 GB of weights streamed per step)"},
+        "k1": {"value": 1000.0 / ms1, "unit": "tokens/s", "ms_per_step": ms1},
+        "hbm_roofline_step": {"bytes_per_step_per_gpu": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": hbm,
+                              "frac": step_gbs / hbm, "peak_kind": peak_kind},
+        "roofline": {"bound": "hbm", "kernel": "qmm_w4a16_kernel", "achieved": q_gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": q_gbs / hbm, "traffic": None, "peak_kind": peak_kind,
+                     "launches_per_step": q["launches"], "ms_per_step": q["ms"]},
+        "kernels_ms": {k: round(v["ms"], 4) for k, v in prof.items()},
+        "e2e": {"value": K / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * (K + 1),
+                "d2h_bytes_per_step": 4 * (K + 1)},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu:
+        v, secs, desc = oracle_sample(K, os.cpu_count() or 1)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": desc}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--k", type=int, default=32)
+    ap.add_argument("--impl", default="iam")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 1)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        if args.impl != "reference":
+            torch.cuda.set_device(local_rank)
+        dist.init_process_group("gloo" if args.impl == "reference" else "nccl",
+                                timeout=datetime.timedelta(seconds=300))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

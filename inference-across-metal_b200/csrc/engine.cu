@@ -1,0 +1,1166 @@
+// The engine behind iam_create / iam_verify: the whole 64-layer decode or
+// K-token verify step of a Qwen3.5-27B-shape model on one GPU (or one
+// tensor-parallel shard), with weights, recurrent state and KV cache resident
+// in HBM and the step captured as one CUDA graph per verify width.
+//
+// Replaces forwardPass (full_forward.swift:1198-1308), which re-reads each
+// layer's weights from mmap and waits on the GPU once per layer, and the
+// MLP-only M-row loop of batch_verify_27b.swift:141-274.
+//
+// Per GDN layer (dispatchGDNLayer, full_forward.swift:993-1161): input RMSNorm,
+// one matmul launch for in_proj_qkv|z|b|a, the fused recurrent kernel, out_proj
+// with the residual add fused, post-norm, gate|up with SwiGLU fused, down with
+// the residual add fused.  Per attention layer (dispatchAttnLayer, 828-987):
+// RMSNorm, q|k|v matmul, q/k-norm + RoPE + KV append, split flash decode,
+// combine + sigmoid gate, o_proj + residual, MLP.  Then final norm, lm_head with
+// an argmax epilogue and the accept-length finalisation.
+#include <dlfcn.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+#include "nccl_shim.h"
+#include "synth.cuh"
+
+namespace iam {
+
+int attn_chunk_tokens();
+
+namespace {
+
+constexpr int kNSplit = 32;     // attention context splits
+constexpr size_t kAlign = 256;  // tensor alignment in the pool
+
+enum class Kind { kQ4Words, kQ4Scales, kQ4Biases, kBf16, kF32 };
+
+// A shard of a tensor: row ranges (concatenated) x one column range, of a
+// [full_rows, full_cols] element grid.
+struct Shard {
+  std::vector<std::pair<int64_t, int64_t>> rows;  // [begin, end)
+  int64_t col0 = 0, col1 = 0;
+  int64_t local_rows() const {
+    int64_t n = 0;
+    for (auto& r : rows) n += r.second - r.first;
+    return n;
+  }
+};
+
+struct TensorRec {
+  std::string name;      // reference tensor name
+  std::string gen_name;  // name of the generator stream
+  Kind kind;
+  int esize;
+  int64_t full_rows, full_cols;  // in stored elements (words for packed codes)
+  Shard shard;
+  void* ptr = nullptr;
+  int syn_kind;
+  float p0 = 0.f, p1 = 0.f;
+  size_t bytes() const { return static_cast<size_t>(shard.local_rows()) * (shard.col1 - shard.col0) * esize; }
+};
+
+struct QW {
+  uint32_t* w = nullptr;
+  uint16_t* s = nullptr;
+  uint16_t* b = nullptr;
+  int rows = 0, cols = 0;  // local output rows, local K
+};
+
+struct Layer {
+  bool attn = false;
+  int idx = 0;  // index among GDN or among attention layers
+  uint16_t* in_norm = nullptr;
+  uint16_t* post_norm = nullptr;
+  QW gate, up, down;
+  // GDN
+  QW qkv, z, bproj, aproj, out;
+  uint16_t* conv_w = nullptr;
+  float* A_log = nullptr;
+  uint16_t* dt_bias = nullptr;
+  uint16_t* norm_w = nullptr;
+  // attention
+  QW q, k, v, o;
+  uint16_t* q_norm = nullptr;
+  uint16_t* k_norm = nullptr;
+};
+
+struct StepIn {  // device copy of the step inputs
+  int32_t pos;
+  int32_t tokens[1];  // [max_rows]
+};
+
+struct ProfEntry {
+  std::string kind;
+  double bytes;
+  cudaEvent_t a, b;
+};
+
+}  // namespace
+
+struct EngineImpl {
+  iam_dims d{};
+  int device = 0, rank = 0, world = 1;
+  cudaStream_t stream = nullptr;
+  void* comm = nullptr;  // ncclComm_t
+  std::string err;
+
+  // shard-local dimensions
+  int gk_l = 0, gv_l = 0, k0 = 0, v0 = 0;            // GDN heads
+  int hq_l = 0, hkv_l = 0, h0 = 0, kv0 = 0;          // attention heads
+  int inter_l = 0, i0 = 0, vocab_l = 0, voff = 0;     // MLP / lm_head
+  int key_l = 0, conv_l = 0, vd_l = 0;
+  int n_gdn = 0, n_attn = 0;
+
+  std::vector<TensorRec> tensors;
+  std::map<std::string, int> by_name;
+  char* pool = nullptr;
+  size_t pool_bytes = 0;
+
+  std::vector<Layer> layers;
+  uint16_t* embed = nullptr;
+  uint16_t* final_norm = nullptr;
+  QW lm;
+
+  // state
+  float* S = nullptr;
+  uint16_t* conv[2] = {nullptr, nullptr};
+  uint16_t* kc = nullptr;
+  uint16_t* vc = nullptr;
+  int* d_parity = nullptr;
+  int parity = 0;
+
+  // activations / workspace
+  int ld_in = 0, ld_attn = 0;
+  uint16_t *hidden = nullptr, *resid = nullptr, *normed = nullptr, *inproj = nullptr, *mid = nullptr,
+           *mlp_h = nullptr, *q_buf = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr, *red32 = nullptr;
+  unsigned long long* keys = nullptr;
+  unsigned long long* best = nullptr;      // [world][max_rows] (TP)
+  int lm_ctas = 0;
+  float* rope_cs = nullptr;
+  StepIn* d_in = nullptr;
+  int32_t* d_out = nullptr;  // [0] accept, [1..] argmax
+  int* d_err = nullptr;
+  StepIn* h_in = nullptr;
+  int32_t* h_out = nullptr;
+
+  std::map<int, cudaGraphExec_t> graphs;
+  int cur_rows = 0;  // verify width of the step being enqueued
+  int host_pos = 0;  // the position the next device-driven step starts at
+  bool pdl = true;
+  std::vector<ProfEntry>* prof = nullptr;
+  int launches = 0;
+
+  int setf(int st, const std::string& m) {
+    err = m;
+    set_error(m);
+    return st;
+  }
+};
+
+namespace {
+
+// ------------------------------------------------------------------ helpers
+int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+int check(EngineImpl& e, int r) {
+  if (r != IAM_OK) e.err = iam_last_error();
+  return r;
+}
+
+#define E_CUDA(call)                                                          \
+  do {                                                                        \
+    cudaError_t e_ = (call);                                                  \
+    if (e_ != cudaSuccess) return e.setf(e_ == cudaErrorMemoryAllocation ? IAM_ENOMEM : IAM_ECUDA, \
+                                         std::string(#call) + ": " + cudaGetErrorString(e_));   \
+  } while (0)
+
+#define E_RUN(call)                      \
+  do {                                   \
+    int r_ = (call);                     \
+    if (r_ != IAM_OK) return check(e, r_); \
+  } while (0)
+
+// Registers one stored tensor.
+void add(EngineImpl& e, const std::string& name, const std::string& gen, Kind kind, int64_t full_rows,
+         int64_t full_cols, Shard sh, int syn, float p0 = 0.f, float p1 = 0.f) {
+  TensorRec t;
+  t.name = name;
+  t.gen_name = gen;
+  t.kind = kind;
+  t.esize = (kind == Kind::kQ4Words || kind == Kind::kF32) ? 4 : 2;
+  t.full_rows = full_rows;
+  t.full_cols = full_cols;
+  if (sh.rows.empty()) sh.rows.push_back({0, full_rows});
+  if (sh.col1 == 0) {
+    sh.col0 = 0;
+    sh.col1 = full_cols;
+  }
+  t.shard = sh;
+  t.syn_kind = syn;
+  t.p0 = p0;
+  t.p1 = p1;
+  e.by_name[name] = static_cast<int>(e.tensors.size());
+  e.tensors.push_back(t);
+}
+
+// A 4-bit matrix [rows, K]: row shard (output features) or K shard (columns).
+void add_q4(EngineImpl& e, const std::string& base, int64_t rows, int64_t K, const Shard& row_shard, int64_t kc0,
+            int64_t kc1) {
+  const int g = e.d.group_size;
+  Shard sw = row_shard, ss = row_shard;
+  if (kc1 > kc0) {
+    sw.col0 = kc0 / 8;
+    sw.col1 = kc1 / 8;
+    ss.col0 = kc0 / g;
+    ss.col1 = kc1 / g;
+  }
+  add(e, base + ".weight", base + ".weight", Kind::kQ4Words, rows, K / 8, sw, SYN_WORDS);
+  add(e, base + ".scales", base + ".scales", Kind::kQ4Scales, rows, K / g, ss, SYN_ABSNORMAL_BF16, 0.02f);
+  add(e, base + ".biases", base + ".scales", Kind::kQ4Biases, rows, K / g, ss, SYN_NEG8_ABSNORMAL_BF16, 0.02f);
+}
+
+Shard rows_of(int64_t b, int64_t en) {
+  Shard s;
+  s.rows.push_back({b, en});
+  return s;
+}
+
+void* tptr(EngineImpl& e, const std::string& name) { return e.tensors[e.by_name.at(name)].ptr; }
+
+QW qw(EngineImpl& e, const std::string& base, int rows, int cols) {
+  QW q;
+  q.w = static_cast<uint32_t*>(tptr(e, base + ".weight"));
+  q.s = static_cast<uint16_t*>(tptr(e, base + ".scales"));
+  q.b = static_cast<uint16_t*>(tptr(e, base + ".biases"));
+  q.rows = rows;
+  q.cols = cols;
+  return q;
+}
+
+int build_registry(EngineImpl& e) {
+  const iam_dims& d = e.d;
+  const int W = e.world, r = e.rank;
+  const int H = d.hidden, I = d.intermediate;
+  const int hd = d.head_dim, gd = d.gdn_dk;
+  const int key_dim = d.gdn_k_heads * gd, vdim = d.gdn_v_heads * d.gdn_dv;
+  const int conv_dim = 2 * key_dim + vdim;
+  // GDN head shards
+  e.gk_l = d.gdn_k_heads / W;
+  e.gv_l = d.gdn_v_heads / W;
+  e.k0 = r * e.gk_l;
+  e.v0 = r * e.gv_l;
+  e.key_l = e.gk_l * gd;
+  e.vd_l = e.gv_l * d.gdn_dv;
+  e.conv_l = 2 * e.key_l + e.vd_l;
+  // attention heads: KV heads split up to n_kv_heads ways, replicated beyond
+  e.hq_l = d.n_heads / W;
+  e.h0 = r * e.hq_l;
+  if (W <= d.n_kv_heads) {
+    e.hkv_l = d.n_kv_heads / W;
+    e.kv0 = r * e.hkv_l;
+  } else {
+    e.hkv_l = 1;
+    e.kv0 = r / (W / d.n_kv_heads);
+  }
+  e.inter_l = I / W;
+  e.i0 = r * e.inter_l;
+  e.vocab_l = d.vocab / W;
+  e.voff = r * e.vocab_l;
+
+  Shard qkv_rows;  // q heads, k heads, v heads of this shard
+  qkv_rows.rows.push_back({e.k0 * gd, (e.k0 + e.gk_l) * gd});
+  qkv_rows.rows.push_back({key_dim + e.k0 * gd, key_dim + (e.k0 + e.gk_l) * gd});
+  qkv_rows.rows.push_back({2 * key_dim + e.v0 * d.gdn_dv, 2 * key_dim + (e.v0 + e.gv_l) * d.gdn_dv});
+  const Shard all;
+
+  add(e, "model.embed_tokens.weight", "model.embed_tokens.weight", Kind::kBf16, d.vocab, H, all, SYN_NORMAL_BF16,
+      0.02f);
+  add(e, "model.norm.weight", "model.norm.weight", Kind::kBf16, 1, H, all, SYN_ONE_PLUS_NORMAL_BF16, 0.02f);
+  add_q4(e, "lm_head", d.vocab, H, rows_of(e.voff, e.voff + e.vocab_l), 0, 0);
+
+  for (int li = 0; li < d.n_layers; ++li) {
+    const std::string p = "model.layers." + std::to_string(li) + ".";
+    const bool attn = (li + 1) % d.full_attn_interval == 0;
+    add(e, p + "input_layernorm.weight", p + "input_layernorm.weight", Kind::kBf16, 1, H, all,
+        SYN_ONE_PLUS_NORMAL_BF16, 0.02f);
+    if (attn) {
+      add_q4(e, p + "self_attn.q_proj", 2 * d.n_heads * hd, H, rows_of(2 * e.h0 * hd, 2 * (e.h0 + e.hq_l) * hd), 0, 0);
+      add_q4(e, p + "self_attn.k_proj", d.n_kv_heads * hd, H, rows_of(e.kv0 * hd, (e.kv0 + e.hkv_l) * hd), 0, 0);
+      add_q4(e, p + "self_attn.v_proj", d.n_kv_heads * hd, H, rows_of(e.kv0 * hd, (e.kv0 + e.hkv_l) * hd), 0, 0);
+      add_q4(e, p + "self_attn.o_proj", H, d.n_heads * hd, all, e.h0 * hd, (e.h0 + e.hq_l) * hd);
+      add(e, p + "self_attn.q_norm.weight", p + "self_attn.q_norm.weight", Kind::kBf16, 1, hd, all,
+          SYN_ONE_PLUS_NORMAL_BF16, 0.02f);
+      add(e, p + "self_attn.k_norm.weight", p + "self_attn.k_norm.weight", Kind::kBf16, 1, hd, all,
+          SYN_ONE_PLUS_NORMAL_BF16, 0.02f);
+    } else {
+      add_q4(e, p + "linear_attn.in_proj_qkv", conv_dim, H, qkv_rows, 0, 0);
+      add_q4(e, p + "linear_attn.in_proj_z", vdim, H, rows_of(e.v0 * d.gdn_dv, (e.v0 + e.gv_l) * d.gdn_dv), 0, 0);
+      add_q4(e, p + "linear_attn.in_proj_b", d.gdn_v_heads, H, rows_of(e.v0, e.v0 + e.gv_l), 0, 0);
+      add_q4(e, p + "linear_attn.in_proj_a", d.gdn_v_heads, H, rows_of(e.v0, e.v0 + e.gv_l), 0, 0);
+      add(e, p + "linear_attn.conv1d.weight", p + "linear_attn.conv1d.weight", Kind::kBf16, conv_dim, d.conv_kernel,
+          qkv_rows, SYN_NORMAL_BF16, 0.1f);
+      add(e, p + "linear_attn.A_log", p + "linear_attn.A_log", Kind::kF32, d.gdn_v_heads, 1,
+          rows_of(e.v0, e.v0 + e.gv_l), SYN_UNIFORM_F32, -1.0f, 2.0f);
+      add(e, p + "linear_attn.dt_bias", p + "linear_attn.dt_bias", Kind::kBf16, d.gdn_v_heads, 1,
+          rows_of(e.v0, e.v0 + e.gv_l), SYN_NORMAL_BF16, 0.1f);
+      add(e, p + "linear_attn.norm.weight", p + "linear_attn.norm.weight", Kind::kBf16, 1, d.gdn_dv, all,
+          SYN_ONE_PLUS_NORMAL_BF16, 0.02f);
+      add_q4(e, p + "linear_attn.out_proj", H, vdim, all, e.v0 * d.gdn_dv, (e.v0 + e.gv_l) * d.gdn_dv);
+    }
+    add(e, p + "post_attention_layernorm.weight", p + "post_attention_layernorm.weight", Kind::kBf16, 1, H, all,
+        SYN_ONE_PLUS_NORMAL_BF16, 0.02f);
+    add_q4(e, p + "mlp.gate_proj", I, H, rows_of(e.i0, e.i0 + e.inter_l), 0, 0);
+    add_q4(e, p + "mlp.up_proj", I, H, rows_of(e.i0, e.i0 + e.inter_l), 0, 0);
+    add_q4(e, p + "mlp.down_proj", H, I, all, e.i0, e.i0 + e.inter_l);
+  }
+  return IAM_OK;
+}
+
+int alloc_all(EngineImpl& e) {
+  const iam_dims& d = e.d;
+  size_t total = 0;
+  for (auto& t : e.tensors) total += (t.bytes() + kAlign - 1) / kAlign * kAlign;
+  e.pool_bytes = total;
+  E_CUDA(cudaMalloc(&e.pool, total));
+  size_t off = 0;
+  for (auto& t : e.tensors) {
+    t.ptr = e.pool + off;
+    off += (t.bytes() + kAlign - 1) / kAlign * kAlign;
+  }
+  // layers
+  e.layers.resize(d.n_layers);
+  const int H = d.hidden;
+  for (int li = 0; li < d.n_layers; ++li) {
+    const std::string p = "model.layers." + std::to_string(li) + ".";
+    Layer& L = e.layers[li];
+    L.attn = (li + 1) % d.full_attn_interval == 0;
+    L.idx = L.attn ? e.n_attn++ : e.n_gdn++;
+    L.in_norm = static_cast<uint16_t*>(tptr(e, p + "input_layernorm.weight"));
+    L.post_norm = static_cast<uint16_t*>(tptr(e, p + "post_attention_layernorm.weight"));
+    L.gate = qw(e, p + "mlp.gate_proj", e.inter_l, H);
+    L.up = qw(e, p + "mlp.up_proj", e.inter_l, H);
+    L.down = qw(e, p + "mlp.down_proj", H, e.inter_l);
+    if (L.attn) {
+      L.q = qw(e, p + "self_attn.q_proj", 2 * e.hq_l * d.head_dim, H);
+      L.k = qw(e, p + "self_attn.k_proj", e.hkv_l * d.head_dim, H);
+      L.v = qw(e, p + "self_attn.v_proj", e.hkv_l * d.head_dim, H);
+      L.o = qw(e, p + "self_attn.o_proj", H, e.hq_l * d.head_dim);
+      L.q_norm = static_cast<uint16_t*>(tptr(e, p + "self_attn.q_norm.weight"));
+      L.k_norm = static_cast<uint16_t*>(tptr(e, p + "self_attn.k_norm.weight"));
+    } else {
+      L.qkv = qw(e, p + "linear_attn.in_proj_qkv", e.conv_l, H);
+      L.z = qw(e, p + "linear_attn.in_proj_z", e.vd_l, H);
+      L.bproj = qw(e, p + "linear_attn.in_proj_b", e.gv_l, H);
+      L.aproj = qw(e, p + "linear_attn.in_proj_a", e.gv_l, H);
+      L.out = qw(e, p + "linear_attn.out_proj", H, e.vd_l);
+      L.conv_w = static_cast<uint16_t*>(tptr(e, p + "linear_attn.conv1d.weight"));
+      L.A_log = static_cast<float*>(tptr(e, p + "linear_attn.A_log"));
+      L.dt_bias = static_cast<uint16_t*>(tptr(e, p + "linear_attn.dt_bias"));
+      L.norm_w = static_cast<uint16_t*>(tptr(e, p + "linear_attn.norm.weight"));
+    }
+  }
+  e.embed = static_cast<uint16_t*>(tptr(e, "model.embed_tokens.weight"));
+  e.final_norm = static_cast<uint16_t*>(tptr(e, "model.norm.weight"));
+  e.lm = qw(e, "lm_head", e.vocab_l, H);
+
+  // state
+  const size_t s_per = static_cast<size_t>(e.gv_l) * d.gdn_dk * d.gdn_dv;
+  E_CUDA(cudaMalloc(&e.S, std::max<size_t>(1, e.n_gdn * s_per) * sizeof(float)));
+  for (int i = 0; i < 2; ++i)
+    E_CUDA(cudaMalloc(&e.conv[i], std::max<size_t>(1, static_cast<size_t>(e.n_gdn) * 3 * e.conv_l) * 2));
+  const size_t kv = static_cast<size_t>(e.n_attn) * d.max_ctx * e.hkv_l * d.head_dim;
+  E_CUDA(cudaMalloc(&e.kc, std::max<size_t>(1, kv) * 2));
+  E_CUDA(cudaMalloc(&e.vc, std::max<size_t>(1, kv) * 2));
+  E_CUDA(cudaMalloc(&e.d_parity, sizeof(int)));
+  E_CUDA(cudaMemset(e.d_parity, 0, sizeof(int)));
+
+  // activations
+  const int R = d.max_rows;
+  e.ld_in = (e.conv_l + e.vd_l + 2 * e.gv_l + 7) / 8 * 8;
+  e.ld_attn = 2 * e.hq_l * d.head_dim + 2 * e.hkv_l * d.head_dim;
+  const int ld_big = std::max(e.ld_in, e.ld_attn);
+  const int ld_mid = std::max(e.vd_l, e.hq_l * d.head_dim);
+  E_CUDA(cudaMalloc(&e.hidden, static_cast<size_t>(R) * H * 2));
+  E_CUDA(cudaMalloc(&e.resid, static_cast<size_t>(R) * H * 2));
+  E_CUDA(cudaMalloc(&e.normed, static_cast<size_t>(R) * H * 2));
+  E_CUDA(cudaMalloc(&e.inproj, static_cast<size_t>(R) * ld_big * 2));
+  E_CUDA(cudaMalloc(&e.mid, static_cast<size_t>(R) * ld_mid * 2));
+  E_CUDA(cudaMalloc(&e.mlp_h, static_cast<size_t>(R) * e.inter_l * 2));
+  E_CUDA(cudaMalloc(&e.q_buf, static_cast<size_t>(R) * e.hq_l * d.head_dim * 2));
+  E_CUDA(cudaMalloc(&e.part_o, static_cast<size_t>(R) * e.hq_l * kNSplit * d.head_dim * 4));
+  E_CUDA(cudaMalloc(&e.part_ml, static_cast<size_t>(R) * e.hq_l * kNSplit * 2 * 4));
+  if (e.world > 1) E_CUDA(cudaMalloc(&e.red32, static_cast<size_t>(R) * H * 4));
+  e.lm_ctas = ceil_div(e.vocab_l, 16);  // at least 16 rows per CTA in every config
+  E_CUDA(cudaMalloc(&e.keys, static_cast<size_t>(e.lm_ctas) * R * 8));
+  E_CUDA(cudaMalloc(&e.best, static_cast<size_t>(e.world) * R * 8));
+  E_CUDA(cudaMalloc(&e.d_in, sizeof(int32_t) * (1 + R)));
+  E_CUDA(cudaMalloc(&e.d_out, sizeof(int32_t) * (1 + R)));
+  E_CUDA(cudaMalloc(&e.d_err, sizeof(int)));
+  E_CUDA(cudaMemset(e.d_err, 0, sizeof(int)));
+  E_CUDA(cudaMallocHost(&e.h_in, sizeof(int32_t) * (1 + R)));
+  E_CUDA(cudaMallocHost(&e.h_out, sizeof(int32_t) * (1 + R)));
+
+  // RoPE table [max_ctx][rotary/2] (cos, sin): precomputeRoPE in double
+  // (full_forward.swift:734-743)
+  std::vector<float> cs(static_cast<size_t>(d.max_ctx) * d.rotary_dim);
+  for (int pos = 0; pos < d.max_ctx; ++pos)
+    for (int i = 0; i < d.rotary_dim / 2; ++i) {
+      const double freq = 1.0 / std::pow(static_cast<double>(d.rope_theta), static_cast<double>(2 * i) / d.rotary_dim);
+      const double ang = static_cast<double>(pos) * freq;
+      cs[static_cast<size_t>(pos) * d.rotary_dim + 2 * i] = static_cast<float>(std::cos(ang));
+      cs[static_cast<size_t>(pos) * d.rotary_dim + 2 * i + 1] = static_cast<float>(std::sin(ang));
+    }
+  E_CUDA(cudaMalloc(&e.rope_cs, cs.size() * 4));
+  E_CUDA(cudaMemcpy(e.rope_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  return IAM_OK;
+}
+
+// ------------------------------------------------------------------ step
+struct Recorder {
+  EngineImpl& e;
+  const char* kind;
+  double bytes;
+  ProfEntry ent;
+  Recorder(EngineImpl& en, const char* k, double b) : e(en), kind(k), bytes(b) {
+    e.launches++;
+    if (e.prof) {
+      ent.kind = k;
+      ent.bytes = b;
+      cudaEventCreate(&ent.a);
+      cudaEventCreate(&ent.b);
+      cudaEventRecord(ent.a, e.stream);
+    }
+  }
+  ~Recorder() {
+    if (e.prof) {
+      cudaEventRecord(ent.b, e.stream);
+      e.prof->push_back(ent);
+    }
+  }
+};
+
+double qbytes(const QW& q) { return static_cast<double>(q.rows) * q.cols * (0.5 + 4.0 / 64.0); }
+
+void seg_of(QmmSeg& s, const QW& q, int mode) {
+  s = QmmSeg{};
+  s.w = q.w;
+  s.s = q.s;
+  s.b = q.b;
+  s.rows = q.rows;
+  s.mode = mode;
+}
+
+int run_qmm(EngineImpl& e, QmmArgs& a, const char* kind, double bytes) {
+  Recorder rec(e, kind, bytes);
+  return qmm_run(a, e.stream, e.pdl);
+}
+
+// Row-parallel matmul (K sharded) followed by the residual add: fused on one
+// GPU; fp32 partials + NCCL all-reduce + residual kernel across GPUs.
+int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, const uint16_t* resid, uint16_t* out);
+
+int enqueue_gdn(EngineImpl& e, const Layer& L, int K) {
+  const iam_dims& d = e.d;
+  const int H = d.hidden;
+  {
+    Recorder rec(e, "rmsnorm", 4.0 * K * H);
+    E_RUN(launch_rms_norm(e.hidden, H, L.in_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
+  }
+  QmmArgs a = {};
+  a.x = e.normed;
+  a.ldx = H;
+  a.M = K;
+  a.K = H;
+  a.nseg = 4;
+  seg_of(a.seg[0], L.qkv, EPI_STORE);
+  a.seg[0].out = e.inproj;
+  seg_of(a.seg[1], L.z, EPI_STORE);
+  a.seg[1].out = e.inproj + e.conv_l;
+  seg_of(a.seg[2], L.bproj, EPI_STORE);
+  a.seg[2].out = e.inproj + e.conv_l + e.vd_l;
+  seg_of(a.seg[3], L.aproj, EPI_STORE);
+  a.seg[3].out = e.inproj + e.conv_l + e.vd_l + e.gv_l;
+  for (int i = 0; i < 4; ++i) a.seg[i].ldo = e.ld_in;
+  E_RUN(run_qmm(e, a, "qmm", qbytes(L.qkv) + qbytes(L.z) + qbytes(L.bproj) + qbytes(L.aproj)));
+
+  GdnArgs g = {};
+  g.in = e.inproj;
+  g.ld_in = e.ld_in;
+  g.z_col = e.conv_l;
+  g.b_col = e.conv_l + e.vd_l;
+  g.a_col = e.conv_l + e.vd_l + e.gv_l;
+  g.conv_w = L.conv_w;
+  const size_t coff = static_cast<size_t>(L.idx) * 3 * e.conv_l;
+  g.conv_in = e.conv[0] + coff;
+  g.conv_out = e.conv[1] + coff;
+  g.parity_dev = e.d_parity;
+  g.A_log = L.A_log;
+  g.dt_bias = L.dt_bias;
+  g.norm_w = L.norm_w;
+  g.S = e.S + static_cast<size_t>(L.idx) * e.gv_l * d.gdn_dk * d.gdn_dv;
+  g.out = e.mid;
+  g.ld_out = e.vd_l;
+  g.n_k_heads = e.gk_l;
+  g.n_v_heads = e.gv_l;
+  g.key_dim = e.key_l;
+  g.conv_dim = e.conv_l;
+  g.rows = K;
+  g.eps = d.eps;
+  {
+    Recorder rec(e, "gdn", 2.0 * e.gv_l * d.gdn_dk * d.gdn_dv * 4 + 2.0 * 3 * e.conv_l * 2);
+    E_RUN(launch_gdn(g, e.stream, e.pdl));
+  }
+  E_RUN(row_parallel_resid(e, L.out, e.mid, e.vd_l, e.hidden, e.resid));
+  return IAM_OK;
+}
+
+int enqueue_attn(EngineImpl& e, const Layer& L, int K) {
+  const iam_dims& d = e.d;
+  const int H = d.hidden, hd = d.head_dim;
+  {
+    Recorder rec(e, "rmsnorm", 4.0 * K * H);
+    E_RUN(launch_rms_norm(e.hidden, H, L.in_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
+  }
+  QmmArgs a = {};
+  a.x = e.normed;
+  a.ldx = H;
+  a.M = K;
+  a.K = H;
+  a.nseg = 3;
+  seg_of(a.seg[0], L.q, EPI_STORE);
+  a.seg[0].out = e.inproj;
+  seg_of(a.seg[1], L.k, EPI_STORE);
+  a.seg[1].out = e.inproj + 2 * e.hq_l * hd;
+  seg_of(a.seg[2], L.v, EPI_STORE);
+  a.seg[2].out = e.inproj + 2 * e.hq_l * hd + e.hkv_l * hd;
+  for (int i = 0; i < 3; ++i) a.seg[i].ldo = e.ld_attn;
+  E_RUN(run_qmm(e, a, "qmm", qbytes(L.q) + qbytes(L.k) + qbytes(L.v)));
+
+  AttnArgs t = {};
+  t.qkv = e.inproj;
+  t.ld_qkv = e.ld_attn;
+  t.k_col = 2 * e.hq_l * hd;
+  t.v_col = 2 * e.hq_l * hd + e.hkv_l * hd;
+  t.q_norm_w = L.q_norm;
+  t.k_norm_w = L.k_norm;
+  const size_t kvoff = static_cast<size_t>(L.idx) * d.max_ctx * e.hkv_l * hd;
+  t.k_cache = e.kc + kvoff;
+  t.v_cache = e.vc + kvoff;
+  t.q_buf = e.q_buf;
+  t.part_o = e.part_o;
+  t.part_ml = e.part_ml;
+  t.out = e.mid;
+  t.ld_out = e.hq_l * hd;
+  t.n_heads = e.hq_l;
+  t.n_kv_heads = e.hkv_l;
+  t.head_dim = hd;
+  t.rotary_dim = d.rotary_dim;
+  t.rope_cs = e.rope_cs;
+  t.max_ctx = d.max_ctx;
+  t.rows = K;
+  t.pos_dev = &e.d_in->pos;
+  t.chunk = attn_chunk_tokens();
+  t.nsplit = kNSplit;
+  t.eps = d.eps;
+  {
+    Recorder rec(e, "attn_prep", 2.0 * K * e.ld_attn);
+    E_RUN(launch_attn_prep(t, e.stream, e.pdl));
+  }
+  {
+    Recorder rec(e, "attn_decode", 0.0);
+    E_RUN(launch_attn_decode(t, e.stream, e.pdl));
+  }
+  {
+    Recorder rec(e, "attn_combine", 4.0 * K * e.hq_l * kNSplit * hd);
+    E_RUN(launch_attn_combine(t, e.stream, e.pdl));
+  }
+  E_RUN(row_parallel_resid(e, L.o, e.mid, e.hq_l * hd, e.hidden, e.resid));
+  return IAM_OK;
+}
+
+int enqueue_mlp(EngineImpl& e, const Layer& L, int K) {
+  const iam_dims& d = e.d;
+  const int H = d.hidden;
+  {
+    Recorder rec(e, "rmsnorm", 4.0 * K * H);
+    E_RUN(launch_rms_norm(e.resid, H, L.post_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
+  }
+  QmmArgs a = {};
+  a.x = e.normed;
+  a.ldx = H;
+  a.M = K;
+  a.K = H;
+  a.nseg = 1;
+  seg_of(a.seg[0], L.gate, EPI_SWIGLU);
+  a.seg[0].w2 = L.up.w;
+  a.seg[0].s2 = L.up.s;
+  a.seg[0].b2 = L.up.b;
+  a.seg[0].out = e.mlp_h;
+  a.seg[0].ldo = e.inter_l;
+  E_RUN(run_qmm(e, a, "qmm", qbytes(L.gate) + qbytes(L.up)));
+  E_RUN(row_parallel_resid(e, L.down, e.mlp_h, e.inter_l, e.resid, e.hidden));
+  return IAM_OK;
+}
+
+__global__ void resid_from_f32_kernel(const float* y, const uint16_t* resid, uint16_t* out, int n) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = f2bf(bf2f(resid[i]) + round_bf(y[i]));
+  pdl_trigger();
+}
+
+__global__ void advance_kernel(StepIn* in, int* parity, int K) {
+  in->pos += K;
+  *parity ^= 1;
+}
+
+
+int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, const uint16_t* resid, uint16_t* out) {
+  const int H = e.d.hidden, M = e.cur_rows;
+  QmmArgs a = {};
+  a.x = x;
+  a.ldx = ldx;
+  a.M = M;
+  a.K = q.cols;
+  a.nseg = 1;
+  if (e.world == 1) {
+    seg_of(a.seg[0], q, EPI_RESID);
+    a.seg[0].out = out;
+    a.seg[0].ldo = H;
+    a.seg[0].resid = resid;
+    a.seg[0].ldr = H;
+    return run_qmm(e, a, "qmm", qbytes(q));
+  }
+  seg_of(a.seg[0], q, EPI_F32);
+  a.seg[0].out32 = e.red32;
+  a.seg[0].ldo = H;
+  E_RUN(run_qmm(e, a, "qmm", qbytes(q)));
+  {
+    Recorder rec(e, "allreduce", 4.0 * M * H);
+    E_RUN(nccl_allreduce_f32(e.comm, e.red32, static_cast<size_t>(M) * H, e.stream));
+  }
+  Recorder rec(e, "resid", 8.0 * M * H);
+  const int n = M * H;
+  return launch_k(resid_from_f32_kernel, dim3(std::min(ceil_div(n, 256), 1184)), dim3(256), 0, e.stream, e.pdl, e.red32,
+                  resid, out, n);
+}
+
+int enqueue_step(EngineImpl& e, int K) {
+  const iam_dims& d = e.d;
+  e.cur_rows = K;
+  {
+    Recorder rec(e, "embed", 4.0 * K * d.hidden);
+    E_RUN(launch_embed_bf16(e.embed, e.d_in->tokens, e.hidden, K, d.hidden, d.vocab, e.d_err, e.stream, false));
+  }
+  for (const Layer& L : e.layers) {
+    if (L.attn) E_RUN(enqueue_attn(e, L, K));
+    else E_RUN(enqueue_gdn(e, L, K));
+    E_RUN(enqueue_mlp(e, L, K));
+  }
+  {
+    Recorder rec(e, "rmsnorm", 4.0 * K * d.hidden);
+    E_RUN(launch_rms_norm(e.hidden, d.hidden, e.final_norm, e.normed, d.hidden, K, d.hidden, d.eps, e.stream, e.pdl));
+  }
+  QmmArgs a = {};
+  a.x = e.normed;
+  a.ldx = d.hidden;
+  a.M = K;
+  a.K = d.hidden;
+  a.nseg = 1;
+  seg_of(a.seg[0], e.lm, EPI_ARGMAX);
+  a.seg[0].keys = e.keys;
+  a.seg[0].key_ld = d.max_rows;
+  a.seg[0].col_base = e.voff;
+  E_RUN(run_qmm(e, a, "qmm", qbytes(e.lm)));
+  // number of lm_head CTAs of the plan (the key rows written)
+  QmmArgs probe = a;
+  probe.M = std::min(K, 32);
+  qmm_plan(probe);
+  const int nparts = probe.total_ctas;
+  if (e.world == 1) {
+    Recorder rec(e, "finalize", 8.0 * nparts * K);
+    E_RUN(launch_finalize(e.keys, nparts, d.max_rows, K, e.d_in->tokens, e.d_out + 1, e.d_out, e.stream, e.pdl));
+  } else {
+    {
+      Recorder rec(e, "finalize", 8.0 * nparts * K);
+      E_RUN(launch_best_keys(e.keys, nparts, d.max_rows, K, e.best + static_cast<size_t>(e.rank) * K, e.stream, e.pdl));
+    }
+    {
+      Recorder rec(e, "allgather", 8.0 * e.world * K);
+      E_RUN(nccl_allgather_u64(e.comm, e.best + static_cast<size_t>(e.rank) * K, e.best, static_cast<size_t>(K),
+                               e.stream));
+    }
+    Recorder rec(e, "finalize", 8.0 * e.world * K);
+    E_RUN(launch_finalize(e.best, e.world, K, K, e.d_in->tokens, e.d_out + 1, e.d_out, e.stream, false));
+  }
+  {
+    Recorder rec(e, "advance", 8.0);
+    advance_kernel<<<1, 1, 0, e.stream>>>(e.d_in, e.d_parity, K);
+    E_CUDA(cudaGetLastError());
+  }
+  return IAM_OK;
+}
+
+int get_graph(EngineImpl& e, int K, cudaGraphExec_t* out) {
+  auto it = e.graphs.find(K);
+  if (it != e.graphs.end()) {
+    *out = it->second;
+    return IAM_OK;
+  }
+  cudaGraph_t g = nullptr;
+  E_CUDA(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
+  const int r = enqueue_step(e, K);
+  cudaGraph_t gg = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(e.stream, &gg);
+  if (r != IAM_OK) {
+    if (gg) cudaGraphDestroy(gg);
+    return r;
+  }
+  E_CUDA(ce);
+  g = gg;
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  E_CUDA(ie);
+  e.graphs[K] = ex;
+  *out = ex;
+  return IAM_OK;
+}
+
+int synth_tensor(EngineImpl& e, const TensorRec& t, uint64_t seed) {
+  SynthJob j = {};
+  j.stream = synth_stream(seed, t.gen_name.c_str());
+  j.kind = t.syn_kind;
+  j.p0 = t.p0;
+  j.p1 = t.p1;
+  j.full_cols = static_cast<uint64_t>(t.full_cols);
+  j.col0 = static_cast<uint64_t>(t.shard.col0);
+  j.width = static_cast<uint64_t>(t.shard.col1 - t.shard.col0);
+  char* dst = static_cast<char*>(t.ptr);
+  for (auto& rr : t.shard.rows) {
+    j.dst = dst;
+    j.row0 = static_cast<uint64_t>(rr.first);
+    j.rows = static_cast<uint64_t>(rr.second - rr.first);
+    E_RUN(synth_fill(j, e.stream));
+    dst += static_cast<size_t>(j.rows) * j.width * t.esize;
+  }
+  return IAM_OK;
+}
+
+}  // namespace
+}  // namespace iam
+
+// ====================================================================== C ABI
+using iam::EngineImpl;
+
+struct iam_engine {
+  EngineImpl impl;
+};
+
+extern "C" void iam_dims_qwen35_27b(iam_dims* d) {
+  d->hidden = 5120;
+  d->intermediate = 17408;
+  d->vocab = 248320;
+  d->n_layers = 64;
+  d->full_attn_interval = 4;
+  d->n_heads = 24;
+  d->n_kv_heads = 4;
+  d->head_dim = 256;
+  d->rotary_dim = 64;
+  d->rope_theta = 1.0e7f;
+  d->gdn_k_heads = 16;
+  d->gdn_v_heads = 48;
+  d->gdn_dk = 128;
+  d->gdn_dv = 128;
+  d->conv_kernel = 4;
+  d->group_size = 64;
+  d->eps = 1e-6f;
+  d->max_ctx = 4608;
+  d->max_rows = 128;
+}
+
+static int validate_dims(const iam_dims& d, int world) {
+  using iam::fail;
+  IAM_CHECK(d.hidden > 0 && d.hidden % 64 == 0, "dims: hidden must be a multiple of 64");
+  IAM_CHECK(d.group_size == 64 && d.conv_kernel == 4, "dims: group_size 64 and conv_kernel 4 required");
+  IAM_CHECK(d.gdn_dk == 128 && d.gdn_dv == 128 && d.head_dim == 256, "dims: GDN head 128 and attention head 256 required");
+  IAM_CHECK(d.rotary_dim % 8 == 0 && d.rotary_dim <= d.head_dim, "dims: rotary_dim must be a multiple of 8");
+  IAM_CHECK(d.full_attn_interval >= 1 && d.n_layers >= 1, "dims: layers");
+  IAM_CHECK(world >= 1 && d.gdn_k_heads % world == 0 && d.gdn_v_heads % world == 0 &&
+                d.gdn_v_heads % d.gdn_k_heads == 0,
+            "dims: GDN heads must split evenly over the GPUs");
+  IAM_CHECK(d.n_heads % world == 0 && d.n_heads % d.n_kv_heads == 0, "dims: query heads must split evenly");
+  IAM_CHECK(world <= d.n_kv_heads ? d.n_kv_heads % world == 0 : world % d.n_kv_heads == 0,
+            "dims: KV heads split or replicate evenly");
+  IAM_CHECK((d.n_heads / world) / std::max(1, world <= d.n_kv_heads ? d.n_kv_heads / world : 1) <= 8,
+            "dims: at most 8 query heads per KV head per GPU");
+  IAM_CHECK(d.intermediate % (64 * world) == 0, "dims: intermediate / world must be a multiple of 64");
+  IAM_CHECK(d.vocab % (16 * world) == 0, "dims: vocab / world must be a multiple of 16");
+  IAM_CHECK(d.max_rows >= 1 && d.max_rows <= iam::kMaxRowsFinalize, "dims: max_rows in 1..256");
+  IAM_CHECK(d.max_ctx >= d.max_rows, "dims: max_ctx");
+  return IAM_OK;
+}
+
+extern "C" int iam_nccl_unique_id(void* id128) { return iam::nccl_unique_id(id128); }
+
+extern "C" int iam_create(const iam_dims* dims, int device, int rank, int world, const void* nccl_id,
+                          iam_engine** out) {
+  using namespace iam;
+  IAM_CHECK(dims && out, "iam_create: null argument");
+  *out = nullptr;
+  int r = validate_dims(*dims, world);
+  if (r != IAM_OK) return r;
+  IAM_CHECK(rank >= 0 && rank < world, "iam_create: rank out of range");
+  IAM_CHECK(world == 1 || nccl_id, "iam_create: an NCCL id is required for world > 1");
+  IAM_CUDA(cudaSetDevice(device));
+  auto* eng = new iam_engine();
+  EngineImpl& e = eng->impl;
+  e.d = *dims;
+  e.device = device;
+  e.rank = rank;
+  e.world = world;
+  const char* pdl = std::getenv("IAM_PDL");
+  e.pdl = !(pdl && pdl[0] == '0');
+  cudaError_t ce = cudaStreamCreateWithFlags(&e.stream, cudaStreamNonBlocking);
+  if (ce != cudaSuccess) {
+    delete eng;
+    return cuda_status(ce, "cudaStreamCreate");
+  }
+  r = build_registry(e);
+  if (r == IAM_OK) r = gdn_init_attrs();  // kernel attributes before any graph capture
+  if (r == IAM_OK) r = attn_init_attrs();
+  if (r == IAM_OK) r = alloc_all(e);
+  if (r == IAM_OK && world > 1) r = nccl_init(&e.comm, nccl_id, rank, world);
+  if (r != IAM_OK) {
+    iam_destroy(eng);
+    return r;
+  }
+  *out = eng;
+  return IAM_OK;
+}
+
+extern "C" void iam_destroy(iam_engine* eng) {
+  if (!eng) return;
+  EngineImpl& e = eng->impl;
+  cudaSetDevice(e.device);
+  if (e.stream) cudaStreamSynchronize(e.stream);
+  for (auto& kv : e.graphs) cudaGraphExecDestroy(kv.second);
+  e.graphs.clear();
+  if (e.comm) iam::nccl_destroy(e.comm);
+  void* bufs[] = {e.pool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
+                  e.mid, e.mlp_h, e.q_buf, e.part_o, e.part_ml, e.red32, e.keys, e.best, e.rope_cs, e.d_in, e.d_out,
+                  e.d_err};
+  for (void* p : bufs)
+    if (p) cudaFree(p);
+  if (e.h_in) cudaFreeHost(e.h_in);
+  if (e.h_out) cudaFreeHost(e.h_out);
+  if (e.stream) cudaStreamDestroy(e.stream);
+  delete eng;
+}
+
+extern "C" const char* iam_engine_error(const iam_engine* eng) { return eng ? eng->impl.err.c_str() : ""; }
+
+extern "C" int iam_load_tensor(iam_engine* eng, const char* name, const void* host_ptr, size_t bytes) {
+  using namespace iam;
+  IAM_CHECK(eng && name && host_ptr, "iam_load_tensor: null argument");
+  EngineImpl& e = eng->impl;
+  auto it = e.by_name.find(name);
+  if (it == e.by_name.end()) return e.setf(IAM_EINVAL, std::string("iam_load_tensor: unknown tensor ") + name);
+  const TensorRec& t = e.tensors[it->second];
+  const size_t full = static_cast<size_t>(t.full_rows) * t.full_cols * t.esize;
+  if (bytes != full)
+    return e.setf(IAM_EINVAL, std::string("iam_load_tensor: ") + name + " expects " + std::to_string(full) + " bytes");
+  E_CUDA(cudaSetDevice(e.device));
+  const char* src = static_cast<const char*>(host_ptr);
+  char* dst = static_cast<char*>(t.ptr);
+  const size_t width = static_cast<size_t>(t.shard.col1 - t.shard.col0) * t.esize;
+  const size_t pitch = static_cast<size_t>(t.full_cols) * t.esize;
+  for (auto& rr : t.shard.rows) {
+    const size_t nrows = static_cast<size_t>(rr.second - rr.first);
+    E_CUDA(cudaMemcpy2DAsync(dst, width, src + rr.first * pitch + t.shard.col0 * t.esize, pitch, width, nrows,
+                             cudaMemcpyHostToDevice, e.stream));
+    dst += nrows * width;
+  }
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  return IAM_OK;
+}
+
+extern "C" int iam_read_tensor(iam_engine* eng, const char* name, void* host_ptr, size_t bytes) {
+  using namespace iam;
+  IAM_CHECK(eng && name && host_ptr, "iam_read_tensor: null argument");
+  EngineImpl& e = eng->impl;
+  E_CUDA(cudaSetDevice(e.device));
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  const std::string n(name);
+  const void* src = nullptr;
+  size_t have = 0;
+  auto it = e.by_name.find(n);
+  if (it != e.by_name.end()) {
+    src = e.tensors[it->second].ptr;
+    have = e.tensors[it->second].bytes();
+  } else if (n.rfind("state.S.", 0) == 0 || n.rfind("state.conv.", 0) == 0 || n.rfind("state.k_cache.", 0) == 0 ||
+             n.rfind("state.v_cache.", 0) == 0) {
+    const int li = std::atoi(n.substr(n.rfind('.') + 1).c_str());
+    if (li < 0 || li >= e.d.n_layers) return e.setf(IAM_EINVAL, "iam_read_tensor: layer out of range");
+    const Layer& L = e.layers[li];
+    if (n.rfind("state.S.", 0) == 0 && !L.attn) {
+      have = static_cast<size_t>(e.gv_l) * e.d.gdn_dk * e.d.gdn_dv * 4;
+      src = e.S + static_cast<size_t>(L.idx) * e.gv_l * e.d.gdn_dk * e.d.gdn_dv;
+    } else if (n.rfind("state.conv.", 0) == 0 && !L.attn) {
+      int par = 0;
+      E_CUDA(cudaMemcpy(&par, e.d_parity, sizeof(int), cudaMemcpyDeviceToHost));
+      have = static_cast<size_t>(3) * e.conv_l * 2;
+      src = e.conv[par] + static_cast<size_t>(L.idx) * 3 * e.conv_l;
+    } else if (L.attn) {
+      have = static_cast<size_t>(e.d.max_ctx) * e.hkv_l * e.d.head_dim * 2;
+      src = (n.rfind("state.k_cache.", 0) == 0 ? e.kc : e.vc) + static_cast<size_t>(L.idx) * e.d.max_ctx * e.hkv_l *
+                                                                    e.d.head_dim;
+    }
+  }
+  if (!src) return e.setf(IAM_EINVAL, std::string("iam_read_tensor: unknown tensor ") + n);
+  if (bytes > have) return e.setf(IAM_EINVAL, "iam_read_tensor: more bytes requested than the tensor holds");
+  E_CUDA(cudaMemcpy(host_ptr, src, bytes, cudaMemcpyDeviceToHost));
+  return IAM_OK;
+}
+
+extern "C" int iam_init_synthetic(iam_engine* eng, uint64_t seed) {
+  using namespace iam;
+  IAM_CHECK(eng, "iam_init_synthetic: null engine");
+  EngineImpl& e = eng->impl;
+  E_CUDA(cudaSetDevice(e.device));
+  for (const TensorRec& t : e.tensors) E_RUN(synth_tensor(e, t, seed));
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  return IAM_OK;
+}
+
+extern "C" int iam_state_reset(iam_engine* eng) {
+  using namespace iam;
+  IAM_CHECK(eng, "iam_state_reset: null engine");
+  EngineImpl& e = eng->impl;
+  E_CUDA(cudaSetDevice(e.device));
+  const size_t s = static_cast<size_t>(e.n_gdn) * e.gv_l * e.d.gdn_dk * e.d.gdn_dv * 4;
+  if (s) E_CUDA(cudaMemsetAsync(e.S, 0, s, e.stream));
+  for (int i = 0; i < 2; ++i)
+    if (e.n_gdn) E_CUDA(cudaMemsetAsync(e.conv[i], 0, static_cast<size_t>(e.n_gdn) * 3 * e.conv_l * 2, e.stream));
+  const size_t kv = static_cast<size_t>(e.n_attn) * e.d.max_ctx * e.hkv_l * e.d.head_dim * 2;
+  if (kv) {
+    E_CUDA(cudaMemsetAsync(e.kc, 0, kv, e.stream));
+    E_CUDA(cudaMemsetAsync(e.vc, 0, kv, e.stream));
+  }
+  E_CUDA(cudaMemsetAsync(e.d_parity, 0, sizeof(int), e.stream));
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  return IAM_OK;
+}
+
+extern "C" int iam_state_init(iam_engine* eng, uint64_t seed, int ctx) {
+  using namespace iam;
+  IAM_CHECK(eng, "iam_state_init: null engine");
+  EngineImpl& e = eng->impl;
+  IAM_CHECK(ctx >= 0 && ctx <= e.d.max_ctx, "iam_state_init: ctx out of range");
+  int r = iam_state_reset(eng);
+  if (r != IAM_OK || seed == 0) return r;
+  const iam_dims& d = e.d;
+  const int gd = d.gdn_dk;
+  const int key_dim = d.gdn_k_heads * gd;
+  const int conv_dim = 2 * key_dim + d.gdn_v_heads * d.gdn_dv;
+  const std::pair<int, int> cr[3] = {{e.k0 * gd, e.gk_l * gd},
+                                     {key_dim + e.k0 * gd, e.gk_l * gd},
+                                     {2 * key_dim + e.v0 * d.gdn_dv, e.gv_l * d.gdn_dv}};
+  for (const Layer& L : e.layers) {
+    const int li = static_cast<int>(&L - e.layers.data());
+    const std::string ls = std::to_string(li);
+    if (L.attn) {
+      if (ctx == 0) continue;
+      for (int kvsel = 0; kvsel < 2; ++kvsel) {
+        SynthJob j = {};
+        j.stream = synth_stream(seed, (std::string(kvsel ? "state.v_cache." : "state.k_cache.") + ls).c_str());
+        j.kind = SYN_NORMAL_BF16;
+        j.p0 = 1.0f;
+        j.full_cols = static_cast<uint64_t>(d.n_kv_heads) * d.head_dim;
+        j.row0 = 0;
+        j.rows = static_cast<uint64_t>(ctx);
+        j.col0 = static_cast<uint64_t>(e.kv0) * d.head_dim;
+        j.width = static_cast<uint64_t>(e.hkv_l) * d.head_dim;
+        j.dst = (kvsel ? e.vc : e.kc) + static_cast<size_t>(L.idx) * d.max_ctx * e.hkv_l * d.head_dim;
+        E_RUN(synth_fill(j, e.stream));
+      }
+    } else {
+      SynthJob j = {};
+      j.stream = synth_stream(seed, ("state.conv." + ls).c_str());
+      j.kind = SYN_NORMAL_BF16;
+      j.p0 = 1.0f;
+      j.full_cols = static_cast<uint64_t>(conv_dim);
+      j.row0 = 0;
+      j.rows = 3;
+      j.dst_ld = static_cast<uint64_t>(e.conv_l);
+      int local = 0;
+      for (auto& c : cr) {
+        j.col0 = static_cast<uint64_t>(c.first);
+        j.width = static_cast<uint64_t>(c.second);
+        j.dst = e.conv[0] + static_cast<size_t>(L.idx) * 3 * e.conv_l + local;
+        E_RUN(synth_fill(j, e.stream));
+        local += c.second;
+      }
+      SynthJob s = {};
+      s.stream = synth_stream(seed, ("state.S." + ls).c_str());
+      s.kind = SYN_NORMAL_F32;
+      s.p0 = 0.01f;
+      s.full_cols = static_cast<uint64_t>(d.gdn_dk) * d.gdn_dv;
+      s.row0 = static_cast<uint64_t>(e.v0);
+      s.rows = static_cast<uint64_t>(e.gv_l);
+      s.col0 = 0;
+      s.width = s.full_cols;
+      s.dst = e.S + static_cast<size_t>(L.idx) * e.gv_l * d.gdn_dk * d.gdn_dv;
+      E_RUN(synth_fill(s, e.stream));
+    }
+  }
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  return IAM_OK;
+}
+
+static int verify_common(iam_engine* eng, int K, int pos) {
+  using namespace iam;
+  IAM_CHECK(eng, "iam_verify: null engine");
+  EngineImpl& e = eng->impl;
+  IAM_CHECK(K >= 1 && K <= e.d.max_rows, "iam_verify: K out of range (1..max_rows)");
+  IAM_CHECK(pos >= 0 && pos + K <= e.d.max_ctx, "iam_verify: pos + K exceeds max_ctx");
+  return IAM_OK;
+}
+
+extern "C" int iam_verify(iam_engine* eng, const int32_t* tokens, int K, int pos, int32_t* argmax_out,
+                          int* accept_len) {
+  using namespace iam;
+  int r = verify_common(eng, K, pos);
+  if (r != IAM_OK) return r;
+  IAM_CHECK(tokens && argmax_out, "iam_verify: null buffer");
+  EngineImpl& e = eng->impl;
+  for (int i = 0; i < K; ++i)
+    if (tokens[i] < 0 || tokens[i] >= e.d.vocab) return e.setf(IAM_EINVAL, "iam_verify: token id out of range");
+  E_CUDA(cudaSetDevice(e.device));
+  cudaGraphExec_t g = nullptr;
+  E_RUN(get_graph(e, K, &g));
+  e.h_in->pos = pos;
+  e.host_pos = pos + K;
+  std::memcpy(e.h_in->tokens, tokens, sizeof(int32_t) * K);
+  E_CUDA(cudaMemcpyAsync(e.d_in, e.h_in, sizeof(int32_t) * (1 + K), cudaMemcpyHostToDevice, e.stream));
+  E_CUDA(cudaGraphLaunch(g, e.stream));
+  E_CUDA(cudaMemcpyAsync(e.h_out, e.d_out, sizeof(int32_t) * (1 + K), cudaMemcpyDeviceToHost, e.stream));
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  std::memcpy(argmax_out, e.h_out + 1, sizeof(int32_t) * K);
+  if (accept_len) *accept_len = e.h_out[0];
+  return IAM_OK;
+}
+
+extern "C" int iam_decode_step(iam_engine* eng, int32_t token, int pos, int32_t* next_token) {
+  int acc = 0;
+  return iam_verify(eng, &token, 1, pos, next_token, &acc);
+}
+
+extern "C" int iam_verify_device(iam_engine* eng, const int32_t* d_tokens, int K, int pos, int32_t* d_argmax,
+                                 void* stream) {
+  using namespace iam;
+  int r = verify_common(eng, K, pos);
+  if (r != IAM_OK) return r;
+  EngineImpl& e = eng->impl;
+  cudaStream_t st = stream ? as_stream(stream) : e.stream;
+  cudaGraphExec_t g = nullptr;
+  E_RUN(get_graph(e, K, &g));
+  // pos < 0 keeps the device position (advanced by the previous step); the
+  // host mirror keeps every step inside the KV cache
+  const int start = pos >= 0 ? pos : e.host_pos;
+  if (start < 0 || start + K > e.d.max_ctx) return e.setf(IAM_EINVAL, "iam_verify_device: pos + K exceeds max_ctx");
+  e.host_pos = start + K;
+  if (pos >= 0) {
+    e.h_in->pos = pos;
+    E_CUDA(cudaMemcpyAsync(&e.d_in->pos, &e.h_in->pos, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  }
+  if (d_tokens) E_CUDA(cudaMemcpyAsync(e.d_in->tokens, d_tokens, sizeof(int32_t) * K, cudaMemcpyDeviceToDevice, st));
+  E_CUDA(cudaGraphLaunch(g, st));
+  if (d_argmax) E_CUDA(cudaMemcpyAsync(d_argmax, e.d_out + 1, sizeof(int32_t) * K, cudaMemcpyDeviceToDevice, st));
+  return IAM_OK;
+}
+
+extern "C" int iam_read_hidden(iam_engine* eng, uint16_t* host_ptr, int K) {
+  using namespace iam;
+  IAM_CHECK(eng && host_ptr && K >= 1, "iam_read_hidden: bad argument");
+  EngineImpl& e = eng->impl;
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  E_CUDA(cudaMemcpy(host_ptr, e.normed, static_cast<size_t>(K) * e.d.hidden * 2, cudaMemcpyDeviceToHost));
+  return IAM_OK;
+}
+
+extern "C" int iam_step_launches(iam_engine* eng, int K) {
+  if (!eng) return -1;
+  EngineImpl& e = eng->impl;
+  // count launches by enqueueing into a throw-away capture
+  cudaGraphExec_t g = nullptr;
+  const int before = e.launches;
+  if (e.graphs.count(K)) {
+    cudaGraphExecDestroy(e.graphs[K]);
+    e.graphs.erase(K);
+  }
+  if (iam::get_graph(e, K, &g) != IAM_OK) return -1;
+  return e.launches - before;
+}
+
+extern "C" double iam_step_bytes(iam_engine* eng, int K, int pos) {
+  if (!eng) return 0.0;
+  EngineImpl& e = eng->impl;
+  const iam_dims& d = e.d;
+  double w = 0.0;
+  for (const auto& t : e.tensors) {
+    if (t.name == "model.embed_tokens.weight") continue;
+    w += static_cast<double>(t.bytes());
+  }
+  w += static_cast<double>(K) * d.hidden * 2;                                            // embedding rows
+  w += 2.0 * e.n_gdn * e.gv_l * d.gdn_dk * d.gdn_dv * 4;                                 // S read + write
+  w += 2.0 * e.n_gdn * 3 * e.conv_l * 2;                                                 // conv state
+  w += 2.0 * e.n_attn * static_cast<double>(pos + K) * e.hkv_l * d.head_dim * 2;         // KV read
+  return w;
+}
+
+extern "C" int iam_profile_step(iam_engine* eng, int K, int pos, int cap, const char** kinds, double* ms,
+                                double* bytes, int* launches) {
+  using namespace iam;
+  int r = verify_common(eng, K, pos);
+  if (r != IAM_OK) return -r;
+  EngineImpl& e = eng->impl;
+  static std::vector<std::string> names;
+  std::vector<ProfEntry> ents;
+  e.h_in->pos = pos;
+  if (cudaMemcpyAsync(&e.d_in->pos, &e.h_in->pos, 4, cudaMemcpyHostToDevice, e.stream) != cudaSuccess) return -IAM_ECUDA;
+  e.prof = &ents;
+  r = enqueue_step(e, K);
+  e.prof = nullptr;
+  if (r != IAM_OK) return -r;
+  if (cudaStreamSynchronize(e.stream) != cudaSuccess) return -IAM_ECUDA;
+  std::vector<std::string> order;
+  std::map<std::string, double> tms, tby;
+  std::map<std::string, int> tn;
+  for (auto& en : ents) {
+    float x = 0.f;
+    cudaEventElapsedTime(&x, en.a, en.b);
+    if (!tn.count(en.kind)) order.push_back(en.kind);
+    tms[en.kind] += x;
+    tby[en.kind] += en.bytes;
+    tn[en.kind] += 1;
+    cudaEventDestroy(en.a);
+    cudaEventDestroy(en.b);
+  }
+  names = order;
+  int n = 0;
+  for (auto& k : names) {
+    if (n >= cap) break;
+    kinds[n] = k.c_str();
+    ms[n] = tms[k];
+    bytes[n] = tby[k];
+    launches[n] = tn[k];
+    ++n;
+  }
+  return n;
+}

@@ -1,0 +1,348 @@
+// GatedDeltaNet recurrent step for K sequential tokens, one CTA per V-head.
+//
+// Fuses, per layer (dispatchGDNLayer, full_forward.swift:1025-1123):
+//   depthwise_conv1d_m1_bf16 -> silu_bf16 -> per_head_rms_norm_scaled_bf16 (q, k)
+//   -> expand_kv_heads_bf16 (index math) -> compute_g_beta_bf16
+//   -> gated_delta_step_bf16 -> rms_norm_gated_bf16
+// with the reference's bf16 rounding points (conv out, SiLU out, q^/k^, g,
+// beta, y, gated-norm out) and its fp32 state.
+//
+// Layout: the head's 128x128 fp32 state lives in registers for the whole
+// verify block (warp w owns rows dv = 8w..8w+7, lane l owns dk = 4l..4l+3);
+// it is read once and written once per step.  Rows of S evolve independently,
+// so the per-token chain needs no block-wide barrier: two 8-row transposed
+// warp reductions (9 shuffles each) and an 8-value broadcast per token.
+// Conv outputs, q^, k^, v, g, beta of a chunk of tokens are prepared in
+// parallel in shared memory before the sequential part; the gated norm runs
+// after it, again in parallel over tokens.
+#include "kernels.cuh"
+
+namespace iam {
+namespace {
+
+constexpr int kHD = 128;      // dk == dv
+constexpr int kThreads = 512; // 16 warps x 8 rows
+constexpr int kChunk = 32;    // tokens prepared per pass
+
+struct GdnSmem {
+  float q[kChunk][kHD];
+  float k[kChunk][kHD];
+  float v[kChunk][kHD];
+  float y[kChunk][kHD];
+  float g[kChunk];
+  float beta[kChunk];
+};
+
+// Sum p[0..7] over the warp; lane l gets the sum of row rr(l) =
+// 4*bit4(l) + 2*bit3(l) + bit2(l).
+__device__ __forceinline__ float reduce8(float (&p)[8], int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = b4 ? p[i] : p[i + 4];
+    const float keep = b4 ? p[i + 4] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b3 ? p[i] : p[i + 2];
+    const float keep = b3 ? p[i + 2] : p[i];
+    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const float send = b2 ? p[0] : p[1];
+    const float keep = b2 ? p[1] : p[0];
+    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  float r = p[0];
+  r += __shfl_xor_sync(0xffffffffu, r, 2);
+  r += __shfl_xor_sync(0xffffffffu, r, 1);
+  return r;
+}
+__device__ __forceinline__ int row_of_lane(int lane) {
+  return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+}
+__device__ __forceinline__ int lane_of_row(int r) { return ((r >> 2) & 1) * 16 + ((r >> 1) & 1) * 8 + (r & 1) * 4; }
+
+// gated_delta_step_bf16 (full_forward.swift:321-355) for tokens [0, n) of the
+// chunk in shared memory: S = g*S; kv = S.k; delta = beta*(v - kv);
+// S = S + k*delta; y = bf16(S.q).  S[r][i] = state[dv = 8w + r][dk = 4l + i].
+__device__ __forceinline__ void delta_chunk(float (&S)[8][4], const GdnSmem& sm, float (*ys)[kHD], int n, int warp,
+                                            int lane) {
+  const int rr = row_of_lane(lane);
+  for (int t = 0; t < n; ++t) {
+    const float gv = sm.g[t], bv = sm.beta[t];
+    const float4 k4 = *reinterpret_cast<const float4*>(&sm.k[t][4 * lane]);
+    const float4 q4 = *reinterpret_cast<const float4*>(&sm.q[t][4 * lane]);
+    float p[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      S[r][0] = S[r][0] * gv;
+      S[r][1] = S[r][1] * gv;
+      S[r][2] = S[r][2] * gv;
+      S[r][3] = S[r][3] * gv;
+      p[r] = fmaf(S[r][3], k4.w, fmaf(S[r][2], k4.z, fmaf(S[r][1], k4.y, S[r][0] * k4.x)));
+    }
+    const float kv = reduce8(p, lane);
+    const float dmine = (sm.v[t][8 * warp + rr] - kv) * bv;
+    float q_part[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float d = __shfl_sync(0xffffffffu, dmine, lane_of_row(r));
+      S[r][0] = S[r][0] + k4.x * d;
+      S[r][1] = S[r][1] + k4.y * d;
+      S[r][2] = S[r][2] + k4.z * d;
+      S[r][3] = S[r][3] + k4.w * d;
+      q_part[r] = fmaf(S[r][3], q4.w, fmaf(S[r][2], q4.z, fmaf(S[r][1], q4.y, S[r][0] * q4.x)));
+    }
+    const float y = reduce8(q_part, lane);
+    if ((lane & 3) == 0) ys[t][8 * warp + rr] = round_bf(y);
+  }
+}
+
+__device__ __forceinline__ void load_state(float (&S)[8][4], const float* Sh, int warp, int lane) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const float4 v = *reinterpret_cast<const float4*>(Sh + (8 * warp + r) * kHD + 4 * lane);
+    S[r][0] = v.x;
+    S[r][1] = v.y;
+    S[r][2] = v.z;
+    S[r][3] = v.w;
+  }
+}
+__device__ __forceinline__ void store_state(const float (&S)[8][4], float* Sh, int warp, int lane) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+    *reinterpret_cast<float4*>(Sh + (8 * warp + r) * kHD + 4 * lane) = make_float4(S[r][0], S[r][1], S[r][2], S[r][3]);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  GdnSmem& sm = *reinterpret_cast<GdnSmem*>(smem_raw);
+  const int h = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rep = a.n_v_heads / a.n_k_heads;
+  const int kh = h / rep;
+  float* Sh = a.S + static_cast<size_t>(h) * kHD * kHD;
+
+  // The state does not depend on the preceding kernel: load it before waiting.
+  float S[8][4];
+  load_state(S, Sh, warp, lane);
+  pdl_wait();
+  const bool swap = a.parity_dev && *a.parity_dev;
+  const uint16_t* conv_in = swap ? a.conv_out : a.conv_in;
+  uint16_t* conv_out = swap ? const_cast<uint16_t*>(a.conv_in) : a.conv_out;
+
+  // conv channel of this thread: 0..127 q (K-head kh), 128..255 k, 256..383 v (V-head h)
+  const int ct = threadIdx.x;
+  int col = -1, region = -1, c = ct & 127;
+  if (ct < 128) {
+    col = kh * kHD + c;
+    region = 0;
+  } else if (ct < 256) {
+    col = a.key_dim + kh * kHD + c;
+    region = 1;
+  } else if (ct < 384) {
+    col = 2 * a.key_dim + h * kHD + c;
+    region = 2;
+  }
+  float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
+  uint16_t w0 = 0, w1 = 0, w2 = 0;  // window: the last three inputs (bf16)
+  if (col >= 0) {
+    const uint16_t* cw = a.conv_w + static_cast<size_t>(col) * 4;
+    k0 = bf2f(cw[0]);
+    k1 = bf2f(cw[1]);
+    k2 = bf2f(cw[2]);
+    k3 = bf2f(cw[3]);
+    w0 = conv_in[col];
+    w1 = conv_in[a.conv_dim + col];
+    w2 = conv_in[2 * a.conv_dim + col];
+  }
+
+  for (int t0 = 0; t0 < a.rows; t0 += kChunk) {
+    const int n = min(kChunk, a.rows - t0);
+    // ---- A: conv + SiLU for the chunk (depthwise_conv1d_m1_bf16, silu_bf16)
+    if (col >= 0) {
+      float* dst = region == 0 ? &sm.q[0][0] : region == 1 ? &sm.k[0][0] : &sm.v[0][0];
+      for (int t = 0; t < n; ++t) {
+        const uint16_t xi = a.in[static_cast<size_t>(t0 + t) * a.ld_in + col];
+        float sum = 0.f;
+        sum = __fadd_rn(sum, __fmul_rn(bf2f(w0), k0));
+        sum = __fadd_rn(sum, __fmul_rn(bf2f(w1), k1));
+        sum = __fadd_rn(sum, __fmul_rn(bf2f(w2), k2));
+        sum = __fadd_rn(sum, __fmul_rn(bf2f(xi), k3));
+        dst[t * kHD + c] = round_bf(silu_f(round_bf(sum)));
+        w0 = w1;
+        w1 = w2;
+        w2 = xi;
+      }
+    } else if (ct - 384 < n) {
+      // ---- g, beta per token (compute_g_beta_bf16)
+      const int t = ct - 384;
+      const size_t row = static_cast<size_t>(t0 + t) * a.ld_in;
+      float gv, bv;
+      g_beta(bf2f(a.in[row + a.a_col + h]), bf2f(a.in[row + a.b_col + h]), a.A_log[h], bf2f(a.dt_bias[h]), gv, bv);
+      sm.g[t] = gv;
+      sm.beta[t] = bv;
+    }
+    __syncthreads();
+    // ---- B: q^ = bf16(q_scale * (q / rms)), k^ likewise (per_head_rms_norm_scaled_bf16)
+    for (int t = warp; t < n; t += kThreads / 32) {
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        float* row = which == 0 ? sm.q[t] : sm.k[t];
+        // GDN_INV_SCALE = Float(0.08838834764) and its fp32 square (full_forward.swift:41, 1056, 1064)
+        const float scale = which == 0 ? __uint_as_float(0x3bffffffu) : __uint_as_float(0x3db504f3u);
+        float4 v = *reinterpret_cast<float4*>(row + 4 * lane);
+        const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+        const float rms = sqrtf(ss / 128.f + 1e-6f);
+        v.x = round_bf(scale * (v.x / rms));
+        v.y = round_bf(scale * (v.y / rms));
+        v.z = round_bf(scale * (v.z / rms));
+        v.w = round_bf(scale * (v.w / rms));
+        *reinterpret_cast<float4*>(row + 4 * lane) = v;
+      }
+    }
+    __syncthreads();
+    // ---- C: the recurrence
+    delta_chunk(S, sm, sm.y, n, warp, lane);
+    __syncthreads();
+    // ---- D: gated RMSNorm (rms_norm_gated_bf16) and store
+    for (int t = warp; t < n; t += kThreads / 32) {
+      const float4 y = *reinterpret_cast<const float4*>(&sm.y[t][4 * lane]);
+      const float ss = warp_sum(y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w);
+      const float rms = sqrtf(ss / 128.f + a.eps);
+      const size_t row = static_cast<size_t>(t0 + t);
+      const uint2 zz = *reinterpret_cast<const uint2*>(a.in + row * a.ld_in + a.z_col + h * kHD + 4 * lane);
+      const uint2 ww = *reinterpret_cast<const uint2*>(a.norm_w + 4 * lane);
+      const float o0 = silu_f(lo_bf(zz.x)) * ((y.x / rms) * lo_bf(ww.x));
+      const float o1 = silu_f(hi_bf(zz.x)) * ((y.y / rms) * hi_bf(ww.x));
+      const float o2 = silu_f(lo_bf(zz.y)) * ((y.z / rms) * lo_bf(ww.y));
+      const float o3 = silu_f(hi_bf(zz.y)) * ((y.w / rms) * hi_bf(ww.y));
+      *reinterpret_cast<uint2*>(a.out + row * a.ld_out + h * kHD + 4 * lane) =
+          make_uint2(pack_bf2(o0, o1), pack_bf2(o2, o3));
+    }
+    __syncthreads();
+  }
+  pdl_trigger();
+  store_state(S, Sh, warp, lane);
+  // new conv state = the last three inputs; q/k channels are shared by the
+  // `rep` V-heads of a K-head, the first of them writes them
+  if (col >= 0 && (region == 2 || h % rep == 0)) {
+    conv_out[col] = w0;
+    conv_out[a.conv_dim + col] = w1;
+    conv_out[2 * a.conv_dim + col] = w2;
+  }
+}
+
+// The operator-level gated_delta_step: q^, k^ (K-head layout), v, g, beta given.
+__global__ void __launch_bounds__(kThreads, 1) gated_delta_kernel(const uint16_t* q, const uint16_t* k,
+                                                                  const uint16_t* v, const uint16_t* g,
+                                                                  const uint16_t* beta, float* Sg, uint16_t* y,
+                                                                  int n_v, int n_k, int rows) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  GdnSmem& sm = *reinterpret_cast<GdnSmem*>(smem_raw);
+  const int h = blockIdx.x, kh = h / (n_v / n_k);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* Sh = Sg + static_cast<size_t>(h) * kHD * kHD;
+  float S[8][4];
+  load_state(S, Sh, warp, lane);
+  for (int t0 = 0; t0 < rows; t0 += kChunk) {
+    const int n = min(kChunk, rows - t0);
+    for (int i = threadIdx.x; i < n * kHD; i += kThreads) {
+      const int t = i / kHD, e = i % kHD;
+      const size_t tr = static_cast<size_t>(t0 + t);
+      sm.q[t][e] = bf2f(q[(tr * n_k + kh) * kHD + e]);
+      sm.k[t][e] = bf2f(k[(tr * n_k + kh) * kHD + e]);
+      sm.v[t][e] = bf2f(v[(tr * n_v + h) * kHD + e]);
+    }
+    if (threadIdx.x < n) {
+      sm.g[threadIdx.x] = bf2f(g[static_cast<size_t>(t0 + threadIdx.x) * n_v + h]);
+      sm.beta[threadIdx.x] = bf2f(beta[static_cast<size_t>(t0 + threadIdx.x) * n_v + h]);
+    }
+    __syncthreads();
+    delta_chunk(S, sm, sm.y, n, warp, lane);
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * kHD; i += kThreads) {
+      const int t = i / kHD, e = i % kHD;
+      y[(static_cast<size_t>(t0 + t) * n_v + h) * kHD + e] = f2bf(sm.y[t][e]);
+    }
+    __syncthreads();
+  }
+  store_state(S, Sh, warp, lane);
+}
+
+bool g_attr_done = false;
+}  // namespace
+
+int gdn_init_attrs();
+namespace {
+int ensure_attrs() { return gdn_init_attrs(); }
+}  // namespace
+
+int gdn_init_attrs() {
+  if (g_attr_done) return IAM_OK;
+  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
+  IAM_CUDA(cudaFuncSetAttribute(gated_delta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
+  g_attr_done = true;
+  return IAM_OK;
+}
+
+int launch_gdn(const GdnArgs& a, cudaStream_t st, bool pdl) {
+  IAM_CHECK(a.n_k_heads > 0 && a.n_v_heads % a.n_k_heads == 0, "gdn: n_v_heads must be a multiple of n_k_heads");
+  IAM_CHECK(a.rows > 0, "gdn: rows must be positive");
+  IAM_CHECK(a.conv_in != a.conv_out, "gdn: conv state in/out must differ");
+  IAM_CHECK(a.ld_in % 4 == 0 && a.z_col % 4 == 0 && a.ld_out % 4 == 0 && aligned16(a.S) && aligned16(a.in),
+            "gdn: 8-byte aligned rows required");
+  const int r = ensure_attrs();
+  if (r != IAM_OK) return r;
+  return launch_k(gdn_fused_kernel, dim3(a.n_v_heads), dim3(kThreads), sizeof(GdnSmem), st, pdl, a);
+}
+
+}  // namespace iam
+
+using namespace iam;
+
+extern "C" int iam_gdn_step_fused(const uint16_t* qkvzab, int ld_in, int z_col, int a_col, int b_col,
+                                  const uint16_t* conv_w, const uint16_t* conv_in, uint16_t* conv_out,
+                                  const float* A_log, const uint16_t* dt_bias, const uint16_t* norm_w, float* S,
+                                  uint16_t* out, int ld_out, int n_k_heads, int n_v_heads, int rows, float eps,
+                                  void* stream) {
+  IAM_CHECK(qkvzab && conv_w && conv_in && conv_out && A_log && dt_bias && norm_w && S && out,
+            "iam_gdn_step_fused: null pointer");
+  GdnArgs a = {};
+  a.in = qkvzab;
+  a.ld_in = ld_in;
+  a.z_col = z_col;
+  a.a_col = a_col;
+  a.b_col = b_col;
+  a.conv_w = conv_w;
+  a.conv_in = conv_in;
+  a.conv_out = conv_out;
+  a.A_log = A_log;
+  a.dt_bias = dt_bias;
+  a.norm_w = norm_w;
+  a.S = S;
+  a.out = out;
+  a.ld_out = ld_out;
+  a.n_k_heads = n_k_heads;
+  a.n_v_heads = n_v_heads;
+  a.key_dim = n_k_heads * kHD;
+  a.conv_dim = 2 * n_k_heads * kHD + n_v_heads * kHD;
+  a.rows = rows;
+  a.eps = eps;
+  return launch_gdn(a, as_stream(stream), false);
+}
+
+extern "C" int iam_gated_delta_step(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* g,
+                                    const uint16_t* beta, float* S, uint16_t* y, int n_v_heads, int n_k_heads, int dk,
+                                    int dv, int rows, void* stream) {
+  IAM_CHECK(q && k && v && g && beta && S && y, "iam_gated_delta_step: null pointer");
+  IAM_CHECK(dk == kHD && dv == kHD, "iam_gated_delta_step: dk == dv == 128 required");
+  IAM_CHECK(n_k_heads > 0 && n_v_heads % n_k_heads == 0 && rows > 0, "iam_gated_delta_step: bad head counts");
+  IAM_CHECK(aligned16(S), "iam_gated_delta_step: S must be 16-byte aligned");
+  const int r = ensure_attrs();
+  if (r != IAM_OK) return r;
+  return launch_k(gated_delta_kernel, dim3(n_v_heads), dim3(kThreads), sizeof(GdnSmem), as_stream(stream), false,
+                  q, k, v, g, beta, S, y, n_v_heads, n_k_heads, rows);
+}

@@ -1,0 +1,384 @@
+// Small kernels of the decode path: norms, element-wise ops, embedding,
+// RoPE, argmax and the verify-block finalisation (operator level + engine).
+#include <cmath>
+
+#include "kernels.cuh"
+
+namespace iam {
+
+// ---------------------------------------------------------------- RMSNorm
+// rms_norm_bf16 (full_forward.swift:59-86) with the reference's exact
+// summation order: 256 threads, thread i sums x[i + 256 j] in order, then the
+// same shared-memory tree; rms = sqrt(sum / dim + eps); out = bf16((x / rms) * w).
+__global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t* __restrict__ x, int ldx,
+                                                       const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
+                                                       int ldo, int dim, float eps) {
+  pdl_wait();
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const uint16_t* xr = x + static_cast<size_t>(row) * ldx;
+  __shared__ float sh[256];
+  float ss = 0.f;
+  for (int i = tid; i < dim; i += 256) {
+    const float v = bf2f(xr[i]);
+    ss += v * v;
+  }
+  sh[tid] = ss;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if (tid < s) sh[tid] += sh[tid + s];
+    __syncthreads();
+  }
+  const float rms = sqrtf(sh[0] / static_cast<float>(dim) + eps);
+  pdl_trigger();
+  uint16_t* orow = out + static_cast<size_t>(row) * ldo;
+  for (int i = tid; i < dim; i += 256) orow[i] = f2bf((bf2f(xr[i]) / rms) * bf2f(w[i]));
+}
+
+int launch_rms_norm(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out, int ldo, int rows, int dim,
+                    float eps, cudaStream_t st, bool pdl) {
+  return launch_k(rms_norm_kernel, dim3(rows), dim3(256), 0, st, pdl, x, ldx, w, out, ldo, dim, eps);
+}
+
+// ---------------------------------------------------------------- element-wise
+__global__ void silu_multiply_kernel(const uint16_t* g, const uint16_t* u, uint16_t* out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = f2bf(silu_f(bf2f(g[i])) * bf2f(u[i]));
+}
+__global__ void residual_add_kernel(const uint16_t* a, const uint16_t* b, uint16_t* out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = f2bf(bf2f(a[i]) + bf2f(b[i]));
+}
+__global__ void sigmoid_gate_kernel(const uint16_t* a, const uint16_t* g, uint16_t* out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = f2bf(bf2f(a[i]) * sigmoid_f(bf2f(g[i])));
+}
+
+static dim3 ew_grid(int n) { return dim3(std::min((n + 255) / 256, 148 * 16)); }
+
+// ---------------------------------------------------------------- embedding
+__global__ void embed_bf16_kernel(const uint16_t* __restrict__ table, const int32_t* __restrict__ tokens,
+                                  uint16_t* __restrict__ out, int hidden, int vocab, int* err) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  int tok = tokens[r];
+  if (tok < 0 || tok >= vocab) {  // never read outside the table; report when asked
+    if (err && threadIdx.x == 0) atomicExch(err, 1);
+    tok = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<size_t>(tok) * hidden);
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(r) * hidden);
+  for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// embed_lookup_bf16 (full_forward.swift:112-133): bf16(float(q) * scale + bias)
+__global__ void embed_q4_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
+                                const uint16_t* __restrict__ b, const int32_t* __restrict__ tokens,
+                                uint16_t* __restrict__ out, int hidden, int group) {
+  const int r = blockIdx.x;
+  const size_t tok = static_cast<size_t>(tokens[r]);
+  const int gpr = hidden / group;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const uint32_t word = w[tok * (hidden / 8) + i / 8];
+    const float q = static_cast<float>((word >> (4 * (i % 8))) & 0xFu);
+    out[static_cast<size_t>(r) * hidden + i] =
+        f2bf(q * bf2f(s[tok * gpr + i / group]) + bf2f(b[tok * gpr + i / group]));
+  }
+}
+
+// ---------------------------------------------------------------- RoPE
+// rope_bf16 + precomputeRoPE (full_forward.swift:148-167, 734-743): angles in
+// double, cos/sin stored fp32, adjacent pairs (2i, 2i+1) rotated in fp32.
+__device__ __forceinline__ void rope_cs(int pos, int i, int rotary, float theta, float& c, float& s) {
+  const double freq = 1.0 / pow(static_cast<double>(theta), static_cast<double>(2 * i) / static_cast<double>(rotary));
+  const double ang = static_cast<double>(pos) * freq;
+  c = static_cast<float>(cos(ang));
+  s = static_cast<float>(sin(ang));
+}
+
+__global__ void rope_kernel(uint16_t* x, int heads, int head_dim, int rotary, float theta, int pos) {
+  const int r = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
+  if (i >= rotary / 2) return;
+  float c, s;
+  rope_cs(pos + r, i, rotary, theta, c, s);
+  uint16_t* p = x + (static_cast<size_t>(r) * heads + h) * head_dim + 2 * i;
+  const float x0 = bf2f(p[0]), x1 = bf2f(p[1]);
+  p[0] = f2bf(x0 * c - x1 * s);
+  p[1] = f2bf(x0 * s + x1 * c);
+}
+
+// ---------------------------------------------------------------- per-head norms
+// per_head_rms_norm_bf16 (full_forward.swift:185-207); the sum runs in index
+// order like the reference's per-thread loop.
+__global__ void per_head_rms_norm_kernel(const uint16_t* x, const uint16_t* w, uint16_t* out, int head_dim,
+                                         float eps) {
+  const size_t base = static_cast<size_t>(blockIdx.x) * head_dim;
+  __shared__ float rms;
+  if (threadIdx.x == 0) {
+    float ss = 0.f;
+    for (int i = 0; i < head_dim; ++i) {
+      const float v = bf2f(x[base + i]);
+      ss += v * v;
+    }
+    rms = sqrtf(ss / static_cast<float>(head_dim) + eps);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < head_dim; e += blockDim.x)
+    out[base + e] = f2bf((bf2f(x[base + e]) / rms) * bf2f(w[e]));
+}
+
+// rms_norm_gated_bf16 (full_forward.swift:357-381)
+__global__ void rms_norm_gated_kernel(const uint16_t* y, const uint16_t* z, const uint16_t* w, uint16_t* out,
+                                      int head_dim, float eps) {
+  const size_t base = static_cast<size_t>(blockIdx.x) * head_dim;
+  __shared__ float rms;
+  if (threadIdx.x == 0) {
+    float ss = 0.f;
+    for (int i = 0; i < head_dim; ++i) {
+      const float v = bf2f(y[base + i]);
+      ss += v * v;
+    }
+    rms = sqrtf(ss / static_cast<float>(head_dim) + eps);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < head_dim; e += blockDim.x) {
+    const float xn = (bf2f(y[base + e]) / rms) * bf2f(w[e]);
+    out[base + e] = f2bf(silu_f(bf2f(z[base + e])) * xn);
+  }
+}
+
+__global__ void g_beta_kernel(const uint16_t* a, const uint16_t* b, const float* A_log, const uint16_t* dt,
+                              uint16_t* g, uint16_t* beta, int rows, int heads) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * heads) return;
+  const int h = i % heads;
+  float gv, bv;
+  g_beta(bf2f(a[i]), bf2f(b[i]), A_log[h], bf2f(dt[h]), gv, bv);
+  g[i] = f2bf(gv);
+  beta[i] = f2bf(bv);
+}
+
+// depthwise_conv1d_m1_bf16 (full_forward.swift:240-263) over `rows` tokens:
+// window [s0, s1, s2, x_t] slides one token at a time.
+__global__ void conv1d_step_kernel(const uint16_t* st_in, const uint16_t* x, const uint16_t* w, uint16_t* out,
+                                   uint16_t* st_out, int C, int rows) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  uint16_t w0 = st_in[c], w1 = st_in[C + c], w2 = st_in[2 * C + c];
+  const float k0 = bf2f(w[4 * c]), k1 = bf2f(w[4 * c + 1]), k2 = bf2f(w[4 * c + 2]), k3 = bf2f(w[4 * c + 3]);
+  for (int r = 0; r < rows; ++r) {
+    const uint16_t xi = x[static_cast<size_t>(r) * C + c];
+    float sum = 0.f;
+    sum += bf2f(w0) * k0;
+    sum += bf2f(w1) * k1;
+    sum += bf2f(w2) * k2;
+    sum += bf2f(xi) * k3;
+    out[static_cast<size_t>(r) * C + c] = f2bf(sum);
+    w0 = w1;
+    w1 = w2;
+    w2 = xi;
+  }
+  st_out[c] = w0;
+  st_out[C + c] = w1;
+  st_out[2 * C + c] = w2;
+}
+
+// ---------------------------------------------------------------- argmax
+// argmax_bf16 (full_forward.swift:169-183): first index of the maximum.
+__global__ void argmax_rows_kernel(const uint16_t* x, int32_t* out, int count) {
+  const uint16_t* row = x + static_cast<size_t>(blockIdx.x) * count;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    const unsigned long long k = argmax_key(bf2f(row[i]), static_cast<uint32_t>(i));
+    best = k > best ? k : best;
+  }
+  __shared__ unsigned long long sh[32];
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+    best = v > best ? v : best;
+  }
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = threadIdx.x < blockDim.x / 32 ? sh[threadIdx.x] : 0ull;
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+      best = v > best ? v : best;
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = static_cast<int32_t>(argmax_key_index(best));
+  }
+}
+
+__device__ __forceinline__ unsigned long long best_key_of_row(const unsigned long long* __restrict__ keys, int nparts,
+                                                             int key_ld, int r, unsigned long long* sh) {
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+    const unsigned long long k = keys[static_cast<size_t>(i) * key_ld + r];
+    best = k > best ? k : best;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+    best = v > best ? v : best;
+  }
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = best;
+  __syncthreads();
+  best = (threadIdx.x & 31) < blockDim.x / 32 ? sh[threadIdx.x & 31] : 0ull;
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+    best = v > best ? v : best;
+  }
+  __syncthreads();
+  return best;
+}
+
+// Verify-block finalisation: reduce the lm_head's per-CTA keys of every row,
+// then the greedy accept length (largest j with tokens[j+1] == argmax[j] for
+// every smaller j; tokens[0] is the token being decoded).
+__global__ void __launch_bounds__(1024) finalize_kernel(const unsigned long long* __restrict__ keys, int nparts,
+                                                        int key_ld, int M, const int32_t* __restrict__ tokens,
+                                                        int32_t* __restrict__ argmax_out, int32_t* accept) {
+  pdl_wait();
+  __shared__ int32_t am[kMaxRowsFinalize];
+  __shared__ unsigned long long sh[32];
+  for (int r = 0; r < M; ++r) {
+    const unsigned long long best = best_key_of_row(keys, nparts, key_ld, r, sh);
+    if (threadIdx.x == 0) {
+      am[r] = static_cast<int32_t>(argmax_key_index(best));
+      argmax_out[r] = am[r];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && accept) {
+    int j = 0;
+    while (j + 1 < M && tokens[j + 1] == am[j]) ++j;
+    *accept = j;
+  }
+}
+
+__global__ void __launch_bounds__(1024) best_keys_kernel(const unsigned long long* __restrict__ keys, int nparts,
+                                                         int key_ld, int M, unsigned long long* best_out) {
+  pdl_wait();
+  __shared__ unsigned long long sh[32];
+  for (int r = 0; r < M; ++r) {
+    const unsigned long long best = best_key_of_row(keys, nparts, key_ld, r, sh);
+    if (threadIdx.x == 0) best_out[r] = best;
+  }
+}
+
+int launch_finalize(const unsigned long long* keys, int nparts, int key_ld, int M, const int32_t* tokens,
+                    int32_t* argmax_out, int32_t* accept, cudaStream_t st, bool pdl) {
+  IAM_CHECK(M <= kMaxRowsFinalize, "finalize: too many rows");
+  return launch_k(finalize_kernel, dim3(1), dim3(1024), 0, st, pdl, keys, nparts, key_ld, M, tokens, argmax_out,
+                  accept);
+}
+
+int launch_best_keys(const unsigned long long* keys, int nparts, int key_ld, int M, unsigned long long* best,
+                     cudaStream_t st, bool pdl) {
+  return launch_k(best_keys_kernel, dim3(1), dim3(1024), 0, st, pdl, keys, nparts, key_ld, M, best);
+}
+
+int launch_embed_bf16(const uint16_t* table, const int32_t* tokens, uint16_t* out, int rows, int hidden, int vocab,
+                      int* err, cudaStream_t st, bool pdl) {
+  return launch_k(embed_bf16_kernel, dim3(rows), dim3(256), 0, st, pdl, table, tokens, out, hidden, vocab, err);
+}
+
+}  // namespace iam
+
+// ====================================================================== C ABI
+using namespace iam;
+
+extern "C" int iam_rms_norm_bf16(const uint16_t* x, const uint16_t* weight, uint16_t* out, int rows, int dim,
+                                 float eps, void* stream) {
+  IAM_CHECK(x && weight && out && rows > 0 && dim > 0, "iam_rms_norm_bf16: bad arguments");
+  return launch_rms_norm(x, dim, weight, out, dim, rows, dim, eps, as_stream(stream), false);
+}
+
+extern "C" int iam_silu_multiply_bf16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int count,
+                                      void* stream) {
+  IAM_CHECK(gate && up && out && count > 0, "iam_silu_multiply_bf16: bad arguments");
+  silu_multiply_kernel<<<ew_grid(count), 256, 0, as_stream(stream)>>>(gate, up, out, count);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_residual_add_bf16(const uint16_t* a, const uint16_t* b, uint16_t* out, int count, void* stream) {
+  IAM_CHECK(a && b && out && count > 0, "iam_residual_add_bf16: bad arguments");
+  residual_add_kernel<<<ew_grid(count), 256, 0, as_stream(stream)>>>(a, b, out, count);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_sigmoid_gate_bf16(const uint16_t* a, const uint16_t* gate, uint16_t* out, int count,
+                                     void* stream) {
+  IAM_CHECK(a && gate && out && count > 0, "iam_sigmoid_gate_bf16: bad arguments");
+  sigmoid_gate_kernel<<<ew_grid(count), 256, 0, as_stream(stream)>>>(a, gate, out, count);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_embed_lookup_q4(const uint32_t* w, const uint16_t* s, const uint16_t* b, const int32_t* tokens,
+                                   uint16_t* out, int rows, int hidden, int group_size, void* stream) {
+  IAM_CHECK(w && s && b && tokens && out && rows > 0, "iam_embed_lookup_q4: bad arguments");
+  IAM_CHECK(hidden % 64 == 0 && group_size == 64, "iam_embed_lookup_q4: hidden % 64 and group 64 required");
+  embed_q4_kernel<<<rows, 256, 0, as_stream(stream)>>>(w, s, b, tokens, out, hidden, group_size);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_embed_lookup_bf16(const uint16_t* table, const int32_t* tokens, uint16_t* out, int rows,
+                                     int hidden, int vocab, void* stream) {
+  IAM_CHECK(table && tokens && out && rows > 0 && hidden % 8 == 0, "iam_embed_lookup_bf16: bad arguments");
+  IAM_CHECK(aligned16(table) && aligned16(out), "iam_embed_lookup_bf16: pointers must be 16-byte aligned");
+  return launch_embed_bf16(table, tokens, out, rows, hidden, vocab, nullptr, as_stream(stream), false);
+}
+
+extern "C" int iam_rope_bf16(uint16_t* x, int rows, int num_heads, int head_dim, int rotary_dim, float theta, int pos,
+                             void* stream) {
+  IAM_CHECK(x && rows > 0 && num_heads > 0 && rotary_dim % 2 == 0 && rotary_dim <= head_dim && rotary_dim <= 2048,
+            "iam_rope_bf16: bad arguments");
+  rope_kernel<<<dim3(rows, num_heads), std::max(32, rotary_dim / 2), 0, as_stream(stream)>>>(x, num_heads, head_dim,
+                                                                                          rotary_dim, theta, pos);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_argmax_bf16(const uint16_t* x, int32_t* out, int rows, int count, void* stream) {
+  IAM_CHECK(x && out && rows > 0 && count > 0, "iam_argmax_bf16: bad arguments");
+  argmax_rows_kernel<<<rows, 1024, 0, as_stream(stream)>>>(x, out, count);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_per_head_rms_norm_bf16(const uint16_t* x, const uint16_t* weight, uint16_t* out, int rows,
+                                          int num_heads, int head_dim, float eps, void* stream) {
+  IAM_CHECK(x && weight && out && rows > 0 && num_heads > 0 && head_dim > 0, "iam_per_head_rms_norm_bf16: bad args");
+  per_head_rms_norm_kernel<<<rows * num_heads, 256, 0, as_stream(stream)>>>(x, weight, out, head_dim, eps);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_rms_norm_gated_bf16(const uint16_t* y, const uint16_t* z, const uint16_t* w, uint16_t* out,
+                                       int rows, int num_heads, int head_dim, float eps, void* stream) {
+  IAM_CHECK(y && z && w && out && rows > 0 && num_heads > 0 && head_dim > 0, "iam_rms_norm_gated_bf16: bad args");
+  rms_norm_gated_kernel<<<rows * num_heads, 128, 0, as_stream(stream)>>>(y, z, w, out, head_dim, eps);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_compute_g_beta(const uint16_t* a, const uint16_t* b, const float* A_log, const uint16_t* dt_bias,
+                                  uint16_t* g, uint16_t* beta, int rows, int n_v_heads, void* stream) {
+  IAM_CHECK(a && b && A_log && dt_bias && g && beta && rows > 0 && n_v_heads > 0, "iam_compute_g_beta: bad args");
+  const int n = rows * n_v_heads;
+  g_beta_kernel<<<(n + 127) / 128, 128, 0, as_stream(stream)>>>(a, b, A_log, dt_bias, g, beta, rows, n_v_heads);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+extern "C" int iam_depthwise_conv1d_step(const uint16_t* state_in, const uint16_t* x, const uint16_t* w,
+                                         uint16_t* out, uint16_t* state_out, int channels, int rows, void* stream) {
+  IAM_CHECK(state_in && x && w && out && state_out && channels > 0 && rows > 0, "iam_depthwise_conv1d_step: bad args");
+  IAM_CHECK(state_in != state_out, "iam_depthwise_conv1d_step: state_out must not alias state_in");
+  conv1d_step_kernel<<<(channels + 255) / 256, 256, 0, as_stream(stream)>>>(state_in, x, w, out, state_out, channels,
+                                                                             rows);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}

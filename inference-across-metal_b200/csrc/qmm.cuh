@@ -1,0 +1,70 @@
+// W4A16 quantized matmul (MLX affine 4-bit, group 64) for decode / verify widths.
+#pragma once
+#include "common.cuh"
+
+namespace iam {
+
+// Epilogues fused into the matmul (full_forward.swift:88-110, 169-183).
+enum QmmEpi : int {
+  EPI_STORE = 0,   // out = bf16(y)
+  EPI_RESID = 1,   // out = bf16(resid + bf16(y))            residual_add_bf16
+  EPI_SWIGLU = 2,  // out = bf16(silu(bf16(gate)) * bf16(up)) silu_multiply_bf16
+  EPI_ARGMAX = 3,  // per-CTA (max bf16(y), first index) keys  argmax_bf16 (partial)
+  EPI_F32 = 4,     // out32 = y (fp32 partial sums, reduced across GPUs next)
+};
+
+struct QmmSeg {
+  const uint32_t* w;   // [rows, K/8] MLX packing
+  const uint16_t* s;   // [rows, K/64] bf16
+  const uint16_t* b;   // [rows, K/64] bf16
+  const uint32_t* w2;  // EPI_SWIGLU: the up matrix (w is gate)
+  const uint16_t* s2;
+  const uint16_t* b2;
+  uint16_t* out;       // out[tok * ldo + col]
+  const uint16_t* resid;
+  unsigned long long* keys;  // EPI_ARGMAX: keys[cta * key_ld + tok], packed (value, index)
+  float* out32;              // EPI_F32
+  int ldo, ldr, key_ld;
+  int rows;       // output columns of this segment (SWIGLU: features)
+  int mode;
+  int cta_begin;  // first blockIdx.x of this segment
+  int col_base;   // EPI_ARGMAX: global column index of local column 0
+};
+
+constexpr int kQmmMaxSeg = 4;
+
+struct QmmArgs {
+  const uint16_t* x;  // x[tok * ldx + k], bf16
+  int ldx;
+  int M;  // tokens
+  int K;  // reduction length, multiple of 64
+  int nseg;
+  int total_ctas;
+  QmmSeg seg[kQmmMaxSeg];
+};
+
+// Tile configuration chosen by the host for a given shape.
+struct QmmConfig {
+  int nt;  // n8 token tiles per pass (1, 2 or 4): tokens per pass = 8*nt
+  int rt;  // 16-row tiles per CTA
+  int kw;  // warps splitting K inside a CTA
+};
+
+// Rows of output handled by one CTA of a segment for a config.
+inline int qmm_rows_per_cta(int mode, int rt) { return (mode == EPI_SWIGLU ? 8 : 16) * rt; }
+
+// Fills cta_begin of each segment and total_ctas; picks the config.
+QmmConfig qmm_plan(QmmArgs& a);
+int qmm_launch(const QmmArgs& a, const QmmConfig& c, cudaStream_t st, bool pdl);
+
+// Order-preserving key: larger float -> larger key; ties -> smaller index wins.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned long long>(0xffffffffu - idx);
+}
+__device__ __forceinline__ uint32_t argmax_key_index(unsigned long long k) {
+  return 0xffffffffu - static_cast<uint32_t>(k & 0xffffffffull);
+}
+
+}  // namespace iam

@@ -118,6 +118,30 @@ def dequant(w, s, b, group: int = 64) -> np.ndarray:
     return bf16(q * sc + bi)
 
 
+_DEQ_CACHE: dict = {}
+
+
+def cache_dequant(enable: bool = True):
+    """Memoise dequant() per weight array (for tests that step a layer many times)."""
+    global _DEQ_ON
+    _DEQ_ON = enable
+    _DEQ_CACHE.clear()
+
+
+_DEQ_ON = False
+
+
+def _dequant_rows(w, s, b, r0, r1, group):
+    if not _DEQ_ON:
+        return dequant(w[r0:r1], s[r0:r1], b[r0:r1], group)
+    key = (id(w), r0, r1)
+    hit = _DEQ_CACHE.get(key)
+    if hit is None or hit[0] is not w:
+        hit = (w, dequant(w[r0:r1], s[r0:r1], b[r0:r1], group))
+        _DEQ_CACHE[key] = hit
+    return hit[1]
+
+
 def qmm_affine4(x, w, s, b, group: int = 64, row_chunk: int = 8192) -> np.ndarray:
     """y[M, N] = bf16(x[M, K] . dequant(W)[N, K]^T), fp32 accumulation.
 
@@ -131,7 +155,7 @@ def qmm_affine4(x, w, s, b, group: int = 64, row_chunk: int = 8192) -> np.ndarra
     y = np.empty((x2.shape[0], n), np.float32)
     for r0 in range(0, n, row_chunk):
         r1 = min(n, r0 + row_chunk)
-        wd = dequant(w[r0:r1], s[r0:r1], b[r0:r1], group)
+        wd = _dequant_rows(w, s, b, r0, r1, group)
         y[:, r0:r1] = x2 @ wd.T
     y = bf16(y)
     return y[0] if squeeze else y

@@ -1,0 +1,230 @@
+"""Engine-level parity on the GPU (the K-token verify entry point).
+
+* device-generated synthetic weights and state == the oracle's, bit for bit;
+* one full-size GDN layer (27B dims) and one full-size attention + MLP layer
+  against the oracle's layer restatement at K = 1 and K > 1;
+* a small model of the same family, K-token verify vs the oracle's model step;
+* K-token verify == K sequential decode steps on the GPU;
+* the GDN recurrence's fp32 state after 256 steps within 1e-4 relative.
+Hidden states within 1e-2 relative / cosine >= 0.9999; argmax identical unless
+the oracle's top two logits are within one bf16 ulp (a tie the two
+accumulation orders may break differently; the margin is reported).
+"""
+import dataclasses
+
+import numpy as np
+import pytest
+
+from oracle import iam_oracle as O
+from oracle import synth_model as SM
+
+from gpu_util import assert_close_bf16, cosine, dev, empty_u16, host_u16, ptr, rel_err
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import iam_b200 as I  # noqa: E402
+
+SEED = 20261201
+
+
+def cdims(d: O.Dims, max_ctx: int, max_rows: int) -> I.Dims:
+    c = I.Dims.qwen35_27b()
+    for f in dataclasses.fields(d):
+        name = {"group": "group_size"}.get(f.name, f.name)
+        setattr(c, name, getattr(d, f.name))
+    c.max_ctx = max_ctx
+    c.max_rows = max_rows
+    return c
+
+
+def check_argmax(got, logits_ref):
+    ref = O.argmax_first(logits_ref)
+    for i, (g, r) in enumerate(zip(got, ref)):
+        if int(g) != int(r):
+            top = float(logits_ref[i, r])
+            ulp = abs(top) * 2.0 ** -7
+            assert float(logits_ref[i, int(g)]) >= top - ulp, f"row {i}: argmax {g} vs {r}, margin > 1 ulp"
+
+
+def run_engine(d: O.Dims, tokens, pos, ctx, max_ctx=None, max_rows=32):
+    e = I.Engine(cdims(d, max_ctx or (pos + len(tokens) + 8), max_rows))
+    e.init_synthetic(SEED)
+    e.state_init(SEED, ctx)
+    am, acc = e.verify(tokens, pos)
+    hid = e.read_hidden(len(tokens))
+    return e, am, acc, hid
+
+
+def oracle_step(d: O.Dims, tokens, pos, ctx, max_ctx):
+    W = SM.make_weights(SEED, d)
+    st = SM.make_state(SEED, d, ctx, max_ctx)
+    am, acc, normed, logits = O.model_step(np.asarray(tokens), pos, W, st, d, return_hidden=True)
+    return W, st, am, acc, normed, logits
+
+
+# ---------------------------------------------------------------- generator
+def test_synthetic_weights_bit_exact():
+    d = O.TINY
+    e = I.Engine(cdims(d, 64, 8))
+    e.init_synthetic(SEED)
+    for li in (0, 3):
+        for name, kind, shape, param in SM.layer_specs(d, li):
+            ref = SM.make_tensor(SEED, name, kind, shape, param)
+            if kind == "q4":
+                w, s, b = ref
+                got_w = e.read_tensor(name + ".weight", w.nbytes).view(np.uint32).reshape(w.shape)
+                got_s = e.read_tensor(name + ".scales", s.size * 2).view(np.uint16)
+                got_b = e.read_tensor(name + ".biases", b.size * 2).view(np.uint16)
+                assert np.array_equal(got_w, w), name
+                assert np.array_equal(got_s, O.to_u16(s).ravel()), name
+                assert np.array_equal(got_b, O.to_u16(b).ravel()), name
+            elif kind == "uniform_f32":
+                got = e.read_tensor(name, ref.size * 4).view(np.float32)
+                assert np.array_equal(got, ref.ravel()), name
+            else:
+                got = e.read_tensor(name, ref.size * 2).view(np.uint16)
+                assert np.array_equal(got, O.to_u16(ref).ravel()), name
+    e.close()
+
+
+def test_seeded_state_bit_exact():
+    d = O.TINY
+    e = I.Engine(cdims(d, 64, 8))
+    e.init_synthetic(SEED)
+    e.state_init(SEED, 20)
+    st = SM.make_state(SEED, d, 20, 64)
+    S0 = e.read_tensor("state.S.0", st.S[0].nbytes).view(np.float32).reshape(st.S[0].shape)
+    assert np.array_equal(S0, st.S[0])
+    c0 = e.read_tensor("state.conv.0", st.conv[0].size * 2).view(np.uint16).reshape(st.conv[0].shape)
+    assert np.array_equal(c0, O.to_u16(st.conv[0]))
+    k3 = e.read_tensor("state.k_cache.3", st.k_cache[3].size * 2).view(np.uint16).reshape(st.k_cache[3].shape)
+    assert np.array_equal(k3, O.to_u16(st.k_cache[3]))
+    e.close()
+
+
+# ---------------------------------------------------------------- one full-size layer
+GDN1 = O.Dims(n_layers=1, vocab=4096)
+ATTN1 = O.Dims(n_layers=1, full_attn_interval=1, vocab=4096)
+
+
+@pytest.mark.parametrize("K", [1, 8, 32])
+def test_one_gdn_layer_27b(K):
+    tokens = SM.draft_tokens(SEED, GDN1, K)
+    e, am, acc, hid = run_engine(GDN1, tokens, 0, 0)
+    W, st, am_ref, acc_ref, normed, logits = oracle_step(GDN1, tokens, 0, 0, 16 + K)
+    assert_close_bf16(hid, normed)
+    check_argmax(am, logits)
+    S = e.read_tensor("state.S.0", st.S[0].nbytes).view(np.float32).reshape(st.S[0].shape)
+    assert rel_err(S, st.S[0]) < 1e-4
+    e.close()
+
+
+@pytest.mark.parametrize("K,pos", [(1, 1023), (4, 1023), (32, 1023)])
+def test_one_attention_layer_27b(K, pos):
+    tokens = SM.draft_tokens(SEED, ATTN1, K)
+    max_ctx = pos + K + 8
+    e, am, acc, hid = run_engine(ATTN1, tokens, pos, pos, max_ctx)
+    W, st, am_ref, acc_ref, normed, logits = oracle_step(ATTN1, tokens, pos, pos, max_ctx)
+    assert_close_bf16(hid, normed)
+    check_argmax(am, logits)
+    kc = e.read_tensor("state.k_cache.0", max_ctx * 4 * 256 * 2).view(np.uint16).reshape(max_ctx, 4, 256)
+    ref_k = O.to_u16(st.k_cache[0])
+    assert np.mean(kc[pos:pos + K] != ref_k[pos:pos + K]) < 0.01  # appended, normed + roped
+    e.close()
+
+
+# ---------------------------------------------------------------- small model, whole step
+@pytest.mark.parametrize("K", [1, 5, 16])
+def test_tiny_model_verify(K):
+    d = O.TINY
+    tokens = SM.draft_tokens(SEED, d, K, tag=f"tiny{K}")
+    pos = 20
+    e, am, acc, hid = run_engine(d, tokens, pos, pos, 64)
+    W, st, am_ref, acc_ref, normed, logits = oracle_step(d, tokens, pos, pos, 64)
+    assert_close_bf16(hid, normed)
+    check_argmax(am, logits)
+    if np.array_equal(am, am_ref):
+        assert acc == acc_ref
+    e.close()
+
+
+def test_accept_length_counts_matching_drafts():
+    d = O.TINY
+    e = I.Engine(cdims(d, 64, 8))
+    e.init_synthetic(SEED)
+    e.state_init(SEED, 10)
+    t0 = np.array([7], np.int32)
+    am1, _ = e.verify(t0, 10)  # greedy next token
+    e.state_init(SEED, 10)
+    toks = np.array([7, am1[0], 3, 3], np.int32)
+    am, acc = e.verify(toks, 10)
+    assert am[0] == am1[0]
+    assert acc >= 1
+    e.close()
+
+
+def test_verify_equals_sequential_decode():
+    d = O.TINY
+    K, pos = 6, 12
+    tokens = SM.draft_tokens(SEED, d, K, tag="seq")
+    e = I.Engine(cdims(d, 64, 8))
+    e.init_synthetic(SEED)
+    e.state_init(SEED, pos)
+    am_block, _ = e.verify(tokens, pos)
+    S_block = e.read_tensor("state.S.0", 6 * 128 * 128 * 4).view(np.float32).copy()
+    e.state_init(SEED, pos)
+    am_seq = []
+    for i in range(K):
+        a, _ = e.verify(tokens[i:i + 1], pos + i)
+        am_seq.append(int(a[0]))
+    S_seq = e.read_tensor("state.S.0", 6 * 128 * 128 * 4).view(np.float32)
+    assert list(am_block) == am_seq
+    assert rel_err(S_block, S_seq) < 1e-5
+    e.close()
+
+
+# ---------------------------------------------------------------- recurrence drift
+def test_gdn_state_256_steps():
+    """The fused GDN kernel over 256 tokens (8 verify blocks of 32) against the
+    oracle's per-token chain: fp32 state within 1e-4 relative."""
+    d = O.QWEN35_27B
+    rng = np.random.default_rng(256)
+    C, HV, HK, VD = d.conv_dim, d.gdn_v_heads, d.gdn_k_heads, d.value_dim
+    ld = C + VD + 2 * HV
+    steps = 256
+    inp = O.bf16(rng.standard_normal((steps, ld)) * 0.5)
+    conv_w = O.bf16(0.1 * rng.standard_normal((C, 4)))
+    A_log = rng.uniform(-1, 1, HV).astype(np.float32)
+    dt_bias = O.bf16(0.1 * rng.standard_normal(HV))
+    norm_w = O.bf16(1 + 0.02 * rng.standard_normal(128))
+    conv0 = O.bf16(rng.standard_normal((3, C)))
+    S0 = (0.01 * rng.standard_normal((HV, 128, 128))).astype(np.float32)
+    # oracle
+    conv = conv0.copy()
+    S = S0.copy()
+    outs = []
+    for t in range(steps):
+        co, conv = O.depthwise_conv1d_step(conv, inp[t, :C], conv_w)
+        cs = O.silu(co)
+        q = O.expand_heads(O.per_head_rms_norm_scaled(cs[:2048].reshape(HK, 128), O.GDN_Q_SCALE), HV)
+        k = O.expand_heads(O.per_head_rms_norm_scaled(cs[2048:4096].reshape(HK, 128), O.GDN_K_SCALE), HV)
+        v = cs[4096:].reshape(HV, 128)
+        g, beta = O.compute_g_beta(inp[t, C + VD + HV:], inp[t, C + VD:C + VD + HV], A_log, dt_bias)
+        y = O.gated_delta_step(q, k, v, g, beta, S)
+        outs.append(O.rms_norm_gated(y, inp[t, C:C + VD].reshape(HV, 128), norm_w).reshape(-1))
+    # GPU, 8 verify blocks of 32 tokens
+    dS = dev(S0.copy(), torch)
+    ca, cb = dev(O.to_u16(conv0), torch), empty_u16(torch, 3, C)
+    out = empty_u16(torch, steps, VD)
+    di = dev(O.to_u16(inp), torch)
+    for blk in range(8):
+        src, dst = (ca, cb) if blk % 2 == 0 else (cb, ca)
+        I.gdn_step_fused(ptr(di) + blk * 32 * ld * 2, ld, C, C + VD + HV, C + VD, ptr(dev(O.to_u16(conv_w), torch)),
+                         ptr(src), ptr(dst), ptr(dev(A_log, torch)), ptr(dev(O.to_u16(dt_bias), torch)),
+                         ptr(dev(O.to_u16(norm_w), torch)), ptr(dS), ptr(out) + blk * 32 * VD * 2, VD, HK, HV, 32)
+    torch.cuda.synchronize()
+    Sg = dS.cpu().numpy()
+    assert rel_err(Sg, S) < 1e-4, rel_err(Sg, S)
+    go = O.from_u16(host_u16(out))
+    assert cosine(go, np.stack(outs)) > 0.9999
