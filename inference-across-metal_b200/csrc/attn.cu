@@ -34,6 +34,7 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 // ---------------------------------------------------------------- prep
 __global__ void __launch_bounds__(256) attn_prep_kernel(const AttnArgs a) {
   pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y * 8 + warp;
@@ -75,7 +76,6 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const AttnArgs a) {
     *reinterpret_cast<uint4*>(a.v_cache + off) =
         *reinterpret_cast<const uint4*>(row + a.v_col + kvh * kHeadDim + 8 * lane);
   }
-  pdl_trigger();
 }
 
 // ---------------------------------------------------------------- decode
@@ -89,6 +89,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
   pdl_wait();
+  pdl_trigger();
   const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
   const int rep = a.n_heads / a.n_kv_heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -165,6 +166,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
 // ---------------------------------------------------------------- combine + gate
 __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
   pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 8 + warp;
@@ -197,7 +199,6 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     for (int i = 0; i < 8; ++i) r[i] = o[i] / l;
   }
   *reinterpret_cast<uint4*>(a.out + static_cast<size_t>(t) * a.ld_out + h * kHeadDim + 8 * lane) = pack8(r);
-  pdl_trigger();
 }
 
 // copy_bf16 x2 (full_forward.swift:384-392, 909-924): append rows of k and v.

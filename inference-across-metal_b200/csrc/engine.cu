@@ -138,6 +138,9 @@ struct EngineImpl {
   uint16_t *hidden = nullptr, *resid = nullptr, *normed = nullptr, *inproj = nullptr, *mid = nullptr,
            *mlp_h = nullptr, *q_buf = nullptr;
   float *part_o = nullptr, *part_ml = nullptr, *red32 = nullptr;
+  float* qws = nullptr;  // split-K workspace of the matmuls (zero between launches)
+  int* qctr = nullptr;
+  size_t qws_floats = 0, qctr_n = 0;
   unsigned long long* keys = nullptr;
   unsigned long long* best = nullptr;      // [world][max_rows] (TP)
   int lm_ctas = 0;
@@ -397,6 +400,19 @@ int alloc_all(EngineImpl& e) {
   if (e.world > 1) E_CUDA(cudaMalloc(&e.red32, static_cast<size_t>(R) * H * 4));
   e.lm_ctas = ceil_div(e.vocab_l, 16);  // at least 16 rows per CTA in every config
   E_CUDA(cudaMalloc(&e.keys, static_cast<size_t>(e.lm_ctas) * R * 8));
+  // split-K workspace: at most (rows / 16) tiles x 128 floats per token tile of
+  // 32 tokens for the widest matrix (lm_head or the fused projections)
+  {
+    const size_t widest = std::max<size_t>({static_cast<size_t>(e.vocab_l), static_cast<size_t>(2 * e.inter_l),
+                                            static_cast<size_t>(e.ld_in), static_cast<size_t>(e.ld_attn),
+                                            static_cast<size_t>(H)});
+    e.qctr_n = (widest / 16 + 64) * 1;
+    e.qws_floats = (widest / 16 + 64) * 4 * 128;
+    E_CUDA(cudaMalloc(&e.qws, e.qws_floats * sizeof(float)));
+    E_CUDA(cudaMalloc(&e.qctr, e.qctr_n * sizeof(int)));
+    E_CUDA(cudaMemset(e.qws, 0, e.qws_floats * sizeof(float)));
+    E_CUDA(cudaMemset(e.qctr, 0, e.qctr_n * sizeof(int)));
+  }
   E_CUDA(cudaMalloc(&e.best, static_cast<size_t>(e.world) * R * 8));
   E_CUDA(cudaMalloc(&e.d_in, sizeof(int32_t) * (1 + R)));
   E_CUDA(cudaMalloc(&e.d_out, sizeof(int32_t) * (1 + R)));
@@ -457,7 +473,9 @@ void seg_of(QmmSeg& s, const QW& q, int mode) {
 
 int run_qmm(EngineImpl& e, QmmArgs& a, const char* kind, double bytes) {
   Recorder rec(e, kind, bytes);
-  return qmm_run(a, e.stream, e.pdl);
+  a.ws = e.qws;
+  a.counters = e.qctr;
+  return qmm_run(a, e.stream, e.pdl, e.qws_floats, e.qctr_n);
 }
 
 // Row-parallel matmul (K sharded) followed by the residual add: fused on one
@@ -609,9 +627,9 @@ int enqueue_mlp(EngineImpl& e, const Layer& L, int K) {
 
 __global__ void resid_from_f32_kernel(const float* y, const uint16_t* resid, uint16_t* out, int n) {
   pdl_wait();
+  pdl_trigger();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     out[i] = f2bf(bf2f(resid[i]) + round_bf(y[i]));
-  pdl_trigger();
 }
 
 __global__ void advance_kernel(StepIn* in, int* parity, int K) {
@@ -854,7 +872,7 @@ extern "C" void iam_destroy(iam_engine* eng) {
   if (e.comm) iam::nccl_destroy(e.comm);
   void* bufs[] = {e.pool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
                   e.mid, e.mlp_h, e.q_buf, e.part_o, e.part_ml, e.red32, e.keys, e.best, e.rope_cs, e.d_in, e.d_out,
-                  e.d_err};
+                  e.d_err, e.qws, e.qctr};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (e.h_in) cudaFreeHost(e.h_in);
@@ -1064,9 +1082,9 @@ extern "C" int iam_decode_step(iam_engine* eng, int32_t token, int pos, int32_t*
 extern "C" int iam_verify_device(iam_engine* eng, const int32_t* d_tokens, int K, int pos, int32_t* d_argmax,
                                  void* stream) {
   using namespace iam;
-  int r = verify_common(eng, K, pos);
-  if (r != IAM_OK) return r;
+  IAM_CHECK(eng, "iam_verify_device: null engine");
   EngineImpl& e = eng->impl;
+  if (K < 1 || K > e.d.max_rows) return e.setf(IAM_EINVAL, "iam_verify_device: K out of range (1..max_rows)");
   cudaStream_t st = stream ? as_stream(stream) : e.stream;
   cudaGraphExec_t g = nullptr;
   E_RUN(get_graph(e, K, &g));

@@ -129,6 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   float S[8][4];
   load_state(S, Sh, warp, lane);
   pdl_wait();
+  pdl_trigger();
   const bool swap = a.parity_dev && *a.parity_dev;
   const uint16_t* conv_in = swap ? a.conv_out : a.conv_in;
   uint16_t* conv_out = swap ? const_cast<uint16_t*>(a.conv_in) : a.conv_out;
@@ -224,7 +225,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
     }
     __syncthreads();
   }
-  pdl_trigger();
   store_state(S, Sh, warp, lane);
   // new conv state = the last three inputs; q/k channels are shared by the
   // `rep` V-heads of a K-head, the first of them writes them

@@ -28,7 +28,9 @@ int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStr
   return IAM_OK;
 }
 
-int qmm_run(QmmArgs a, cudaStream_t st, bool pdl);
+// a.ws == nullptr: use the library's split-K workspace; else a.ws/a.counters
+// hold at least ws_floats_cap floats / ws_ctr_cap counters, all zero.
+int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap = 0, size_t ws_ctr_cap = 0);
 
 int launch_rms_norm(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out, int ldo, int rows, int dim,
                     float eps, cudaStream_t st, bool pdl);

@@ -13,15 +13,20 @@ namespace iam {
 __global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t* __restrict__ x, int ldx,
                                                        const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
                                                        int ldo, int dim, float eps) {
+  constexpr int kMaxPer = 32;  // dim <= 256 * 32 keeps the row in registers
   pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
   const uint16_t* xr = x + static_cast<size_t>(row) * ldx;
   __shared__ float sh[256];
+  float v[kMaxPer];
+  const int n = (dim - tid + 255) / 256;  // elements of this thread: tid, tid + 256, ...
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) v[j] = j < n ? bf2f(xr[tid + 256 * j]) : 0.f;  // all loads in flight
   float ss = 0.f;
-  for (int i = tid; i < dim; i += 256) {
-    const float v = bf2f(xr[i]);
-    ss += v * v;
-  }
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j)
+    if (j < n) ss += v[j] * v[j];  // the reference's order: x[tid], x[tid + 256], ...
   sh[tid] = ss;
   __syncthreads();
   for (int s = 128; s > 0; s >>= 1) {
@@ -29,13 +34,15 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t* __restric
     __syncthreads();
   }
   const float rms = sqrtf(sh[0] / static_cast<float>(dim) + eps);
-  pdl_trigger();
   uint16_t* orow = out + static_cast<size_t>(row) * ldo;
-  for (int i = tid; i < dim; i += 256) orow[i] = f2bf((bf2f(xr[i]) / rms) * bf2f(w[i]));
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j)
+    if (j < n) orow[tid + 256 * j] = f2bf((v[j] / rms) * bf2f(w[tid + 256 * j]));
 }
 
 int launch_rms_norm(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out, int ldo, int rows, int dim,
                     float eps, cudaStream_t st, bool pdl) {
+  IAM_CHECK(dim <= 256 * 32, "rms_norm: dim <= 8192 required");
   return launch_k(rms_norm_kernel, dim3(rows), dim3(256), 0, st, pdl, x, ldx, w, out, ldo, dim, eps);
 }
 
@@ -59,6 +66,7 @@ static dim3 ew_grid(int n) { return dim3(std::min((n + 255) / 256, 148 * 16)); }
 __global__ void embed_bf16_kernel(const uint16_t* __restrict__ table, const int32_t* __restrict__ tokens,
                                   uint16_t* __restrict__ out, int hidden, int vocab, int* err) {
   pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   int tok = tokens[r];
   if (tok < 0 || tok >= vocab) {  // never read outside the table; report when asked
@@ -237,6 +245,7 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const unsigned long long
                                                         int key_ld, int M, const int32_t* __restrict__ tokens,
                                                         int32_t* __restrict__ argmax_out, int32_t* accept) {
   pdl_wait();
+  pdl_trigger();
   __shared__ int32_t am[kMaxRowsFinalize];
   __shared__ unsigned long long sh[32];
   for (int r = 0; r < M; ++r) {
@@ -257,6 +266,7 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const unsigned long long
 __global__ void __launch_bounds__(1024) best_keys_kernel(const unsigned long long* __restrict__ keys, int nparts,
                                                          int key_ld, int M, unsigned long long* best_out) {
   pdl_wait();
+  pdl_trigger();
   __shared__ unsigned long long sh[32];
   for (int r = 0; r < M; ++r) {
     const unsigned long long best = best_key_of_row(keys, nparts, key_ld, r, sh);

@@ -1,5 +1,7 @@
 // W4A16 quantized matmul (MLX affine 4-bit, group 64) for decode / verify widths.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace iam {
@@ -40,14 +42,39 @@ struct QmmArgs {
   int K;  // reduction length, multiple of 64
   int nseg;
   int total_ctas;
+  int chunk;      // 64-groups per staged x chunk
+  int xrows;      // token rows of a staged x chunk
+  int ws_blocks;  // row blocks (CTAs along x) of the split-K workspace
+  float* ws;      // split-K partial sums (zero between launches)
+  int* counters;  // split-K arrival counters (zero between launches)
+  int* err;       // device error word (a bounded wait that gave up writes IAM_ETIMEOUT)
   QmmSeg seg[kQmmMaxSeg];
 };
 
 // Tile configuration chosen by the host for a given shape.
 struct QmmConfig {
-  int nt;  // n8 token tiles per pass (1, 2 or 4): tokens per pass = 8*nt
-  int rt;  // 16-row tiles per CTA
-  int kw;  // warps splitting K inside a CTA
+  int nt;     // n8 token tiles per pass (1, 2 or 4): tokens per pass = 8*nt
+  int rt;     // 16-row tiles per CTA (one warp each)
+  int ks;     // CTAs splitting K (partials summed in an fp32 workspace)
+  int kp;     // weight groups in flight per warp
+  int chunk;  // 64-groups per staged x chunk
+  bool tma;   // weights through the TMA ring (else register loads)
+};
+// Split-K workspace needed by a plan: floats and counters.
+size_t qmm_ws_floats(const QmmArgs& a, const QmmConfig& c);
+size_t qmm_ws_counters(const QmmArgs& a, const QmmConfig& c);
+constexpr int kQmmMaxSmem = 200 * 1024;
+
+// Tensor maps of one segment for the TMA variant: packed codes [rows, K/2]
+// uint8 (box 16 or 8 rows x 128 bytes, 128B swizzle), scales and biases
+// [rows, K/64] uint16 (box 16 or 8 rows x 8 groups).  SwiGLU segments use
+// 8-row boxes of the gate (w, s, b) and up (w2, s2, b2) matrices.
+struct QmmTmaMaps {
+  CUtensorMap w, s, b, w2, s2, b2;
+};
+struct QmmTmaArgs {
+  QmmArgs a;
+  QmmTmaMaps maps[kQmmMaxSeg];
 };
 
 // Rows of output handled by one CTA of a segment for a config.

@@ -92,9 +92,8 @@ def exported_symbols():
 
 def _check(status: int, engine=None):
     if status != IAM_OK:
-        if engine is not None:
-            msg = lib().iam_engine_error(engine).decode()
-        else:
+        msg = lib().iam_engine_error(engine).decode() if engine is not None else ""
+        if not msg:
             msg = lib().iam_last_error().decode()
         raise IamError(status, msg)
 

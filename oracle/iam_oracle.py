@@ -109,13 +109,19 @@ def unpack_codes(w: np.ndarray) -> np.ndarray:
     return q.reshape(*w.shape[:-1], w.shape[-1] * 8).astype(np.uint8)
 
 
+# Diagnostic switch for tests: keep the dequantised weight in fp32 instead of
+# rounding it to bf16 as mx.dequantize does.
+EXACT_DEQUANT = False
+
+
 def dequant(w, s, b, group: int = 64) -> np.ndarray:
     """MLX affine dequant to bf16: w = bf16(q * scale + bias), computed in fp32
     (float(nibble) * scale + bias, full_forward.swift:129-132)."""
     q = unpack_codes(w).astype(np.float32)
     sc = np.repeat(np.asarray(s, np.float32), group, axis=-1)
     bi = np.repeat(np.asarray(b, np.float32), group, axis=-1)
-    return bf16(q * sc + bi)
+    v = (q * sc + bi).astype(np.float32)
+    return v if EXACT_DEQUANT else bf16(v)
 
 
 _DEQ_CACHE: dict = {}

@@ -2,9 +2,10 @@
 restatement and the reference's own kernels (golden vectors).
 
 Tolerances: element-wise kernels bit-exact against the reference's golden
-outputs; the quantized matmul within 1e-2 relative error and cosine >= 0.9999
-(the oracle dequantises to bf16 like mx.dequantize, the kernel keeps the
-dequantised weight exact in fp32); reductions within one bf16 ulp.
+outputs (exp/log may differ by an ulp on a few elements); the quantized matmul
+within 1e-2 relative error and cosine >= 0.9999 (both sides multiply with the
+bf16 weights of mx.dequantize; only the fp32 accumulation order differs);
+reductions within one bf16 ulp.
 """
 import numpy as np
 import pytest
@@ -51,8 +52,8 @@ def test_qmm_down_proj_shape():
     x = synth.gen_normal_bf16(14, "t.qmm.down.x", M * K, 3.0).astype(np.float32).reshape(M, K)
     ref = O.qmm_affine4(x, w, s.astype(np.float32), b.astype(np.float32))
     y = empty_u16(torch, M, N)
-    I.qmm_affine4(ptr(dev(w, torch)), ptr(dev(s.view(np.uint16), torch)), ptr(dev(b.view(np.uint16), torch)),
-                  ptr(dev(u(x), torch)), ptr(y), M, N, K)
+    keep = [dev(w, torch), dev(s.view(np.uint16), torch), dev(b.view(np.uint16), torch), dev(u(x), torch)]
+    I.qmm_affine4(*[ptr(t) for t in keep], ptr(y), M, N, K)
     sync()
     assert_close_bf16(host_u16(y), ref)
 
@@ -92,8 +93,8 @@ def test_elementwise_golden(golden):
 def test_embed_lookup_golden(golden):
     toks = dev(golden["embed.tokens"].astype(np.int32), torch)
     out = empty_u16(torch, 3, 5120)
-    I.embed_lookup_q4(ptr(dev(golden["embed.w"], torch)), ptr(dev(golden["embed.s"], torch)),
-                      ptr(dev(golden["embed.b"], torch)), ptr(toks), ptr(out), 3, 5120)
+    keep = [dev(golden[k], torch) for k in ("embed.w", "embed.s", "embed.b")]
+    I.embed_lookup_q4(*[ptr(t) for t in keep], ptr(toks), ptr(out), 3, 5120)
     sync()
     assert np.array_equal(host_u16(out), golden["embed.out"])
 
@@ -108,20 +109,21 @@ def test_rope_golden(golden):
 
 def test_argmax_golden(golden):
     out = torch.zeros(1, dtype=torch.int32, device="cuda")
-    I.argmax_bf16(ptr(dev(golden["argmax.x"], torch)), ptr(out), 1, golden["argmax.x"].size)
+    x = dev(golden["argmax.x"], torch)
+    I.argmax_bf16(ptr(x), ptr(out), 1, golden["argmax.x"].size)
     sync()
     assert int(out.item()) == int(golden["argmax.out"][0])
 
 
 def test_norms_golden(golden):
     out = empty_u16(torch, 24, 256)
-    I.per_head_rms_norm_bf16(ptr(dev(golden["rope.x"], torch)), ptr(dev(golden["phnorm.w"], torch)), ptr(out), 1, 24,
-                             256)
+    x, w = dev(golden["rope.x"], torch), dev(golden["phnorm.w"], torch)
+    I.per_head_rms_norm_bf16(ptr(x), ptr(w), ptr(out), 1, 24, 256)
     sync()
     assert np.array_equal(host_u16(out), golden["phnorm.out"])
     out = empty_u16(torch, 48, 128)
-    I.rms_norm_gated_bf16(ptr(dev(golden["gnorm.y"], torch)), ptr(dev(golden["gnorm.z"], torch)),
-                          ptr(dev(golden["gnorm.w"], torch)), ptr(out), 1, 48, 128)
+    keep = [dev(golden[k], torch) for k in ("gnorm.y", "gnorm.z", "gnorm.w")]
+    I.rms_norm_gated_bf16(*[ptr(t) for t in keep], ptr(out), 1, 48, 128)
     sync()
     got, ref = host_u16(out), golden["gnorm.out"]
     assert np.mean(got != ref) < 0.01
@@ -130,15 +132,14 @@ def test_norms_golden(golden):
 def test_conv_gbeta_golden(golden):
     C = golden["conv.x"].size
     out, ns = empty_u16(torch, C), empty_u16(torch, 3, C)
-    I.depthwise_conv1d_step(ptr(dev(golden["conv.state"], torch)), ptr(dev(golden["conv.x"], torch)),
-                            ptr(dev(golden["conv.w"], torch)), ptr(out), ptr(ns), C, 1)
+    keep = [dev(golden[k], torch) for k in ("conv.state", "conv.x", "conv.w")]
+    I.depthwise_conv1d_step(*[ptr(t) for t in keep], ptr(out), ptr(ns), C, 1)
     sync()
     assert np.array_equal(host_u16(out), golden["conv.out"])
     assert np.array_equal(host_u16(ns), golden["conv.new_state"])
     g, beta = empty_u16(torch, 48), empty_u16(torch, 48)
-    I.compute_g_beta(ptr(dev(golden["gb.a"], torch)), ptr(dev(golden["gb.b"], torch)),
-                     ptr(dev(golden["gb.A_log"], torch)), ptr(dev(golden["gb.dt_bias"], torch)), ptr(g), ptr(beta), 1,
-                     48)
+    keep = [dev(golden[k], torch) for k in ("gb.a", "gb.b", "gb.A_log", "gb.dt_bias")]
+    I.compute_g_beta(*[ptr(t) for t in keep], ptr(g), ptr(beta), 1, 48)
     sync()
     assert np.mean(host_u16(g) != golden["gb.g"]) <= 2 / 48
     assert np.mean(host_u16(beta) != golden["gb.beta"]) <= 2 / 48
@@ -151,9 +152,8 @@ def test_gated_delta_sequence_golden(golden):
     k = golden["delta.k"][:, :1, :].copy()
     S = dev(golden["delta.S0"].copy(), torch)
     y = empty_u16(torch, T, HV, 128)
-    I.gated_delta_step(ptr(dev(q, torch)), ptr(dev(k, torch)), ptr(dev(golden["delta.v"], torch)),
-                       ptr(dev(golden["delta.g"], torch)), ptr(dev(golden["delta.beta"], torch)), ptr(S), ptr(y), HV, 1,
-                       128, 128, T)
+    keep = [dev(q, torch), dev(k, torch)] + [dev(golden[n], torch) for n in ("delta.v", "delta.g", "delta.beta")]
+    I.gated_delta_step(*[ptr(t) for t in keep], ptr(S), ptr(y), HV, 1, 128, 128, T)
     sync()
     Sg = S.cpu().numpy()
     ref = golden["delta.S"]
@@ -175,8 +175,8 @@ def test_sdpa_decode_append(pos, rows):
     vn = O.bf16(rng.standard_normal((rows, hkv, hd)))
     dk, dv = dev(u(kc), torch), dev(u(vc), torch)
     out = empty_u16(torch, rows, hq, hd)
-    I.sdpa_decode_append(ptr(dev(u(q), torch)), ptr(dev(u(kn), torch)), ptr(dev(u(vn), torch)), ptr(dk), ptr(dv),
-                         ptr(out), rows, pos, hq, hkv, hd, max_ctx)
+    keep = [dev(u(q), torch), dev(u(kn), torch), dev(u(vn), torch)]
+    I.sdpa_decode_append(*[ptr(t) for t in keep], ptr(dk), ptr(dv), ptr(out), rows, pos, hq, hkv, hd, max_ctx)
     sync()
     kref, vref = kc.copy(), vc.copy()
     kref[pos:pos + rows] = kn
