@@ -79,10 +79,16 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const AttnArgs a) {
 }
 
 // ---------------------------------------------------------------- decode
+// One CTA per (context split, KV head, block of kRowBlock verify rows): the
+// split's 32-key chunks are staged once in shared memory and serve every
+// (row, query head) pair of the block; warp w owns pairs w, w + 8, ...
+constexpr int kRowBlock = 8;
+constexpr int kMaxPairs = 8;  // pairs per warp: kRowBlock * 8 query heads / 8 warps
+
 struct DecodeSmem {
   uint16_t k[kChunkTok][kKvStride];
   uint16_t v[kChunkTok][kKvStride];
-  float q[8][kHeadDim];
+  uint16_t q[kRowBlock * 8][kHeadDim];
 };
 
 __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
@@ -90,32 +96,39 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
   pdl_wait();
   pdl_trigger();
-  const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
+  const int split = blockIdx.x, kvh = blockIdx.y, t0 = blockIdx.z * kRowBlock;
   const int rep = a.n_heads / a.n_kv_heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int last = min(cur_pos(a) + t, a.max_ctx - 1);  // attends to positions 0..last
-  const int nch = last / kChunkTok + 1;
+  const int nrows = min(kRowBlock, a.rows - t0);
+  const int npairs = nrows * rep;
+  const int pos0 = cur_pos(a);
+  // the block's longest context decides its chunk range; shorter rows mask
+  const int last_max = min(pos0 + t0 + nrows - 1, a.max_ctx - 1);
+  const int nch = last_max / kChunkTok + 1;
   const int c_begin = static_cast<int>((static_cast<long long>(split) * nch) / a.nsplit);
   const int c_end = static_cast<int>((static_cast<long long>(split + 1) * nch) / a.nsplit);
-  const int h = kvh * rep + min(warp, rep - 1);
-  if (warp < rep) {
-    float qf[8];
-    unpack8(*reinterpret_cast<const uint4*>(a.q_buf + (static_cast<size_t>(t) * a.n_heads + h) * kHeadDim + 8 * lane),
-            qf);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) sm.q[warp][8 * lane + i] = qf[i];
+  for (int i = threadIdx.x; i < npairs * (kHeadDim / 8); i += blockDim.x) {
+    const int pr = i / (kHeadDim / 8), d8 = (i % (kHeadDim / 8)) * 8;
+    const int t = t0 + pr / rep, h = kvh * rep + pr % rep;
+    *reinterpret_cast<uint4*>(&sm.q[pr][d8]) =
+        *reinterpret_cast<const uint4*>(a.q_buf + (static_cast<size_t>(t) * a.n_heads + h) * kHeadDim + d8);
   }
-  // running softmax state of this warp's query: max, sum, o[8 * lane .. 8 * lane + 7]
-  float m_run = -INFINITY, l_run = 0.f;
-  float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float m_run[kMaxPairs], l_run[kMaxPairs], o[kMaxPairs][8];
+#pragma unroll
+  for (int pp = 0; pp < kMaxPairs; ++pp) {
+    m_run[pp] = -INFINITY;
+    l_run[pp] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[pp][i] = 0.f;
+  }
   for (int c = c_begin; c < c_end; ++c) {
     const int p0 = c * kChunkTok;
-    const int nvalid = min(kChunkTok, last - p0 + 1);
-    __syncthreads();  // previous chunk consumed
+    const int nstage = min(kChunkTok, last_max - p0 + 1);
+    __syncthreads();  // previous chunk consumed (and q staged on the first pass)
     for (int i = threadIdx.x; i < kChunkTok * (kHeadDim / 8); i += blockDim.x) {
       const int r = i / (kHeadDim / 8), d8 = (i % (kHeadDim / 8)) * 8;
       uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (r < nvalid) {
+      if (r < nstage) {
         const size_t off = (static_cast<size_t>(p0 + r) * a.n_kv_heads + kvh) * kHeadDim + d8;
         kk = *reinterpret_cast<const uint4*>(a.k_cache + off);
         vv = *reinterpret_cast<const uint4*>(a.v_cache + off);
@@ -124,42 +137,57 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
       *reinterpret_cast<uint4*>(&sm.v[r][d8]) = vv;
     }
     __syncthreads();
-    if (warp < rep) {
-      float s = 0.f;  // lane = key
-      for (int d = 0; d < kHeadDim; d += 8) {
-        float kf[8];
-        unpack8(*reinterpret_cast<const uint4*>(&sm.k[lane][d]), kf);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) s = fmaf(sm.q[warp][d + i], kf[i], s);
+    for (int pp = 0; pp < kMaxPairs; ++pp) {
+      const int pr = warp + 8 * pp;
+      if (pr < npairs) {
+        const int t = t0 + pr / rep;
+        const int nvalid = min(kChunkTok, min(pos0 + t, a.max_ctx - 1) - p0 + 1);  // causal
+        if (nvalid > 0) {
+          float s = 0.f;  // lane = key
+          for (int d = 0; d < kHeadDim; d += 8) {
+            float kf[8], qf[8];
+            unpack8(*reinterpret_cast<const uint4*>(&sm.k[lane][d]), kf);
+            unpack8(*reinterpret_cast<const uint4*>(&sm.q[pr][d]), qf);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s = fmaf(qf[i], kf[i], s);
+          }
+          s *= 0.0625f;  // 1/sqrt(256)
+          float mc = lane < nvalid ? s : -INFINITY;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
+          const float m_new = fmaxf(m_run[pp], mc);
+          const float keep = expf(m_run[pp] - m_new);  // 0 on the first chunk
+          const float p = lane < nvalid ? expf(s - m_new) : 0.f;
+          l_run[pp] = l_run[pp] * keep + warp_sum(p);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[pp][i] *= keep;
+          for (int j = 0; j < nvalid; ++j) {
+            const float pj = __shfl_sync(0xffffffffu, p, j);
+            float vf[8];
+            unpack8(*reinterpret_cast<const uint4*>(&sm.v[j][8 * lane]), vf);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[pp][i] = fmaf(pj, vf[i], o[pp][i]);
+          }
+          m_run[pp] = m_new;
+        }
       }
-      s *= 0.0625f;  // 1/sqrt(256)
-      float mc = lane < nvalid ? s : -INFINITY;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
-      const float m_new = fmaxf(m_run, mc);
-      const float keep = expf(m_run - m_new);  // 0 on the first chunk
-      const float p = lane < nvalid ? expf(s - m_new) : 0.f;
-      l_run = l_run * keep + warp_sum(p);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] *= keep;
-      for (int j = 0; j < nvalid; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, p, j);
-        float vf[8];
-        unpack8(*reinterpret_cast<const uint4*>(&sm.v[j][8 * lane]), vf);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = fmaf(pj, vf[i], o[i]);
-      }
-      m_run = m_new;
     }
   }
-  if (warp >= rep) return;
-  const size_t part = (static_cast<size_t>(t) * a.n_heads + h) * a.nsplit + split;
-  float4* po = reinterpret_cast<float4*>(a.part_o + part * kHeadDim + 8 * lane);
-  po[0] = make_float4(o[0], o[1], o[2], o[3]);
-  po[1] = make_float4(o[4], o[5], o[6], o[7]);
-  if (lane == 0) {
-    a.part_ml[2 * part] = m_run;  // -inf for an empty split
-    a.part_ml[2 * part + 1] = l_run;
+#pragma unroll
+  for (int pp = 0; pp < kMaxPairs; ++pp) {
+    const int pr = warp + 8 * pp;
+    if (pr < npairs) {
+      const int t = t0 + pr / rep, h = kvh * rep + pr % rep;
+      const size_t part = (static_cast<size_t>(t) * a.n_heads + h) * a.nsplit + split;
+      float4* po = reinterpret_cast<float4*>(a.part_o + part * kHeadDim + 8 * lane);
+      po[0] = make_float4(o[pp][0], o[pp][1], o[pp][2], o[pp][3]);
+      po[1] = make_float4(o[pp][4], o[pp][5], o[pp][6], o[pp][7]);
+      if (lane == 0) {
+        a.part_ml[2 * part] = m_run[pp];  // -inf when the split saw no key of this row
+        a.part_ml[2 * part + 1] = l_run[pp];
+      }
+    }
   }
 }
 
@@ -171,16 +199,24 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 8 + warp;
   if (h >= a.n_heads) return;
-  const int nch = a.nsplit;  // splits
-  const size_t base = (static_cast<size_t>(t) * a.n_heads + h) * a.nsplit;
-  float mx = -INFINITY;
-  for (int c = 0; c < nch; ++c) mx = fmaxf(mx, a.part_ml[2 * (base + c)]);
-  float l = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int c = 0; c < nch; ++c) {
-    const float mc = a.part_ml[2 * (base + c)];
-    if (mc == -INFINITY) continue;  // empty split
-    const float sc = expf(mc - mx);
-    l = fmaf(a.part_ml[2 * (base + c) + 1], sc, l);
+  const int ns = a.nsplit;  // <= 64
+  const size_t base = (static_cast<size_t>(t) * a.n_heads + h) * ns;
+  // lane i holds split i and i + 32: max, then each split's weight exp(m_i - max)
+  const float m0 = lane < ns ? a.part_ml[2 * (base + lane)] : -INFINITY;
+  const float m1 = lane + 32 < ns ? a.part_ml[2 * (base + lane + 32)] : -INFINITY;
+  float mx = fmaxf(m0, m1);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float sc0 = m0 == -INFINITY ? 0.f : expf(m0 - mx);
+  const float sc1 = m1 == -INFINITY ? 0.f : expf(m1 - mx);
+  float l = (lane < ns ? a.part_ml[2 * (base + lane) + 1] * sc0 : 0.f) +
+            (lane + 32 < ns ? a.part_ml[2 * (base + lane + 32) + 1] * sc1 : 0.f);
+  l = warp_sum(l);
+  float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+  for (int c = 0; c < ns; ++c) {
+    const float sc = __shfl_sync(0xffffffffu, c < 32 ? sc0 : sc1, c & 31);
+    if (sc == 0.f) continue;
     const float4* po = reinterpret_cast<const float4*>(a.part_o + (base + c) * kHeadDim + 8 * lane);
     const float4 x0 = po[0], x1 = po[1];
     o[0] = fmaf(x0.x, sc, o[0]); o[1] = fmaf(x0.y, sc, o[1]); o[2] = fmaf(x0.z, sc, o[2]); o[3] = fmaf(x0.w, sc, o[3]);
@@ -247,8 +283,9 @@ int launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   IAM_CHECK(a.n_heads % a.n_kv_heads == 0 && a.n_heads / a.n_kv_heads <= 8, "attention: GQA group of at most 8");
   const int r = attn_init_attrs();
   if (r != IAM_OK) return r;
-  return launch_k(attn_decode_kernel, dim3(a.nsplit, a.n_kv_heads, a.rows), dim3(256), sizeof(DecodeSmem), st,
-                  pdl, a);
+  IAM_CHECK(a.nsplit >= 1 && a.nsplit <= 64, "attention: 1..64 context splits");
+  return launch_k(attn_decode_kernel, dim3(a.nsplit, a.n_kv_heads, (a.rows + kRowBlock - 1) / kRowBlock), dim3(256),
+                  sizeof(DecodeSmem), st, pdl, a);
 }
 
 int launch_attn_combine(const AttnArgs& a, cudaStream_t st, bool pdl) {

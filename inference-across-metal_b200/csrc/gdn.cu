@@ -162,20 +162,28 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
 
   for (int t0 = 0; t0 < a.rows; t0 += kChunk) {
     const int n = min(kChunk, a.rows - t0);
-    // ---- A: conv + SiLU for the chunk (depthwise_conv1d_m1_bf16, silu_bf16)
+    // ---- A: conv + SiLU for the chunk (depthwise_conv1d_m1_bf16, silu_bf16);
+    // all of the chunk's inputs are loaded before the sequential window
     if (col >= 0) {
       float* dst = region == 0 ? &sm.q[0][0] : region == 1 ? &sm.k[0][0] : &sm.v[0][0];
-      for (int t = 0; t < n; ++t) {
-        const uint16_t xi = a.in[static_cast<size_t>(t0 + t) * a.ld_in + col];
-        float sum = 0.f;
-        sum = __fadd_rn(sum, __fmul_rn(bf2f(w0), k0));
-        sum = __fadd_rn(sum, __fmul_rn(bf2f(w1), k1));
-        sum = __fadd_rn(sum, __fmul_rn(bf2f(w2), k2));
-        sum = __fadd_rn(sum, __fmul_rn(bf2f(xi), k3));
-        dst[t * kHD + c] = round_bf(silu_f(round_bf(sum)));
-        w0 = w1;
-        w1 = w2;
-        w2 = xi;
+      uint16_t xin[kChunk];
+#pragma unroll
+      for (int t = 0; t < kChunk; ++t)
+        xin[t] = t < n ? a.in[static_cast<size_t>(t0 + t) * a.ld_in + col] : uint16_t(0);
+#pragma unroll
+      for (int t = 0; t < kChunk; ++t) {
+        if (t < n) {
+          const uint16_t xi = xin[t];
+          float sum = 0.f;
+          sum = __fadd_rn(sum, __fmul_rn(bf2f(w0), k0));
+          sum = __fadd_rn(sum, __fmul_rn(bf2f(w1), k1));
+          sum = __fadd_rn(sum, __fmul_rn(bf2f(w2), k2));
+          sum = __fadd_rn(sum, __fmul_rn(bf2f(xi), k3));
+          dst[t * kHD + c] = round_bf(silu_f(round_bf(sum)));
+          w0 = w1;
+          w1 = w2;
+          w2 = xi;
+        }
       }
     } else if (ct - 384 < n) {
       // ---- g, beta per token (compute_g_beta_bf16)

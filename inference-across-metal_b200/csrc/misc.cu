@@ -7,43 +7,73 @@
 namespace iam {
 
 // ---------------------------------------------------------------- RMSNorm
-// rms_norm_bf16 (full_forward.swift:59-86) with the reference's exact
-// summation order: 256 threads, thread i sums x[i + 256 j] in order, then the
-// same shared-memory tree; rms = sqrt(sum / dim + eps); out = bf16((x / rms) * w).
-__global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t* __restrict__ x, int ldx,
+// rms_norm_bf16 (full_forward.swift:59-86), bit-exact with the reference's
+// summation order: the reference's thread i (of 256) sums x[i + 256 j] in j
+// order, then a shared-memory tree adds thread i + s into i for s = 128..1.
+// Here warp 0 plays all 256 threads: lane l owns virtual threads 8l..8l+7 and
+// reads them with one 16-byte load per j; tree levels s >= 8 are lane
+// shuffles (xor 16..1), s = 4, 2, 1 are in-lane.  rms = sqrt(sum / dim + eps);
+// then the whole CTA writes out = bf16((x / rms) * w) with 16-byte accesses.
+// Requires dim % 256 == 0.
+__global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restrict__ x, int ldx,
                                                        const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
                                                        int ldo, int dim, float eps) {
-  constexpr int kMaxPer = 32;  // dim <= 256 * 32 keeps the row in registers
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
   const uint16_t* xr = x + static_cast<size_t>(row) * ldx;
-  __shared__ float sh[256];
-  float v[kMaxPer];
-  const int n = (dim - tid + 255) / 256;  // elements of this thread: tid, tid + 256, ...
+  __shared__ float rms_s;
+  if (tid < 32) {
+    float p[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int nj = dim / 256;
+    for (int j = 0; j < nj; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + 256 * j + 8 * tid);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int j = 0; j < kMaxPer; ++j) v[j] = j < n ? bf2f(xr[tid + 256 * j]) : 0.f;  // all loads in flight
-  float ss = 0.f;
+      for (int i = 0; i < 4; ++i) {
+        const float a0 = lo_bf(u[i]), a1 = hi_bf(u[i]);
+        p[2 * i] += a0 * a0;
+        p[2 * i + 1] += a1 * a1;
+      }
+    }
 #pragma unroll
-  for (int j = 0; j < kMaxPer; ++j)
-    if (j < n) ss += v[j] * v[j];  // the reference's order: x[tid], x[tid + 256], ...
-  sh[tid] = ss;
-  __syncthreads();
-  for (int s = 128; s > 0; s >>= 1) {
-    if (tid < s) sh[tid] += sh[tid + s];
-    __syncthreads();
+    for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float other = __shfl_xor_sync(0xffffffffu, p[i], o);
+        if (tid < o) p[i] += other;  // lanes >= o only feed lower lanes
+      }
+    if (tid == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) p[i] += p[i + 4];
+      p[0] += p[2];
+      p[1] += p[3];
+      p[0] += p[1];
+      rms_s = sqrtf(p[0] / static_cast<float>(dim) + eps);
+    }
   }
-  const float rms = sqrtf(sh[0] / static_cast<float>(dim) + eps);
+  __syncthreads();
+  const float rms = rms_s;
   uint16_t* orow = out + static_cast<size_t>(row) * ldo;
+  for (int i = tid; i < dim / 8; i += blockDim.x) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + 8 * i);
+    const uint4 ww = *reinterpret_cast<const uint4*>(w + 8 * i);
+    const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, wv[4] = {ww.x, ww.y, ww.z, ww.w};
+    uint32_t o[4];
 #pragma unroll
-  for (int j = 0; j < kMaxPer; ++j)
-    if (j < n) orow[tid + 256 * j] = f2bf((v[j] / rms) * bf2f(w[tid + 256 * j]));
+    for (int k = 0; k < 4; ++k)
+      o[k] = pack_bf2((lo_bf(xv[k]) / rms) * lo_bf(wv[k]), (hi_bf(xv[k]) / rms) * hi_bf(wv[k]));
+    *reinterpret_cast<uint4*>(orow + 8 * i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 int launch_rms_norm(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out, int ldo, int rows, int dim,
                     float eps, cudaStream_t st, bool pdl) {
-  IAM_CHECK(dim <= 256 * 32, "rms_norm: dim <= 8192 required");
-  return launch_k(rms_norm_kernel, dim3(rows), dim3(256), 0, st, pdl, x, ldx, w, out, ldo, dim, eps);
+  IAM_CHECK(dim % 256 == 0, "rms_norm: dim must be a multiple of 256");
+  IAM_CHECK(aligned16(x) && aligned16(w) && aligned16(out) && ldx % 8 == 0 && ldo % 8 == 0,
+            "rms_norm: 16-byte aligned rows required");
+  return launch_k(rms_norm_kernel, dim3(rows), dim3(std::min(512, std::max(32, dim / 8))), 0, st, pdl, x, ldx, w, out,
+                  ldo, dim, eps);
 }
 
 // ---------------------------------------------------------------- element-wise

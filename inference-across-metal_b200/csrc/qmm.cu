@@ -492,17 +492,16 @@ __global__ void __launch_bounds__(32 * RT) qmm_tma_kernel(const __grid_constant_
   for (int j = 0; j < NT; ++j)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
-  bool xok[NT];
+  // fragment addresses inside a stage (128B swizzle: 16-byte chunk ^= row & 7):
+  // group q of the stage sits in box q >> 2, chunk 2 (q & 3) + (t >> 1)
+  int wofs[4];
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) wofs[q4] = g * 128 + (((2 * q4 + (t >> 1)) ^ (g & 7)) << 4) + (t & 1) * 8;
+  // token rows past M read row 0: their MMA columns are never stored
   int xoff[NT];
 #pragma unroll
-  for (int j = 0; j < NT; ++j) {
-    xok[j] = 8 * j + g < mt;
-    xoff[j] = (xok[j] ? 8 * j + g : 0) * tstride + t * 32;
-  }
-  // fragment addresses inside a stage (128B swizzle: chunk ^= row & 7)
-  const int sw = g & 7;
-  const int wofs0 = g * 128 + (t & 1) * 8;
-  const int wofs1 = (g + 8) * 128 + (t & 1) * 8;
+  for (int j = 0; j < NT; ++j) xoff[j] = (8 * j + g < mt ? 8 * j + g : 0) * tstride + t * 32;
+  const int sofs0 = 4096 + g * 16, sofs1 = 4096 + (g + 8) * 16;
   bool ok = true;
 
   int blk = 0;
@@ -518,46 +517,42 @@ __global__ void __launch_bounds__(32 * RT) qmm_tma_kernel(const __grid_constant_
       __syncwarp();
       if (ok) {
         const unsigned char* sp = ring + st * kStageBytes;
+        const unsigned char* xq = xb + (blk * 8 - c * cgmax) * 128;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const int chunk = ((2 * (q & 3) + (t >> 1)) ^ sw) << 4;
-          const unsigned char* wb = sp + (q >> 2) * 2048 + chunk;
-          const uint2 wa = *reinterpret_cast<const uint2*>(wb + wofs0);
-          const uint2 wc = *reinterpret_cast<const uint2*>(wb + wofs1);
-          const uint32_t sa = *reinterpret_cast<const uint16_t*>(sp + 4096 + g * 16 + q * 2) |
-                              (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(sp + 4352 + g * 16 + q * 2))
-                               << 16);
-          const uint32_t sbv =
-              *reinterpret_cast<const uint16_t*>(sp + 4096 + (g + 8) * 16 + q * 2) |
-              (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(sp + 4352 + (g + 8) * 16 + q * 2)) << 16);
-          const int cl = blk * 8 + q - c * cgmax;  // group inside the staged x chunk
-          uint4 xb0[NT], xb1[NT];
+          const unsigned char* wb = sp + (q >> 2) * 2048 + wofs[q & 3];
+          const uint2 wa = *reinterpret_cast<const uint2*>(wb);         // row g:   words 2t, 2t+1
+          const uint2 wc = *reinterpret_cast<const uint2*>(wb + 1024);  // row g+8
+          const uint32_t sg = *reinterpret_cast<const uint16_t*>(sp + sofs0 + q * 2);
+          const uint32_t bg = *reinterpret_cast<const uint16_t*>(sp + sofs0 + 256 + q * 2);
+          const uint32_t sh = *reinterpret_cast<const uint16_t*>(sp + sofs1 + q * 2);
+          const uint32_t bh = *reinterpret_cast<const uint16_t*>(sp + sofs1 + 256 + q * 2);
+          // (s, s), (s/16, s/16) exact, (b, b) for rows g and g+8
+          const uint32_t s2a = sg * 0x10001u, b2a = bg * 0x10001u;  // (s, s), (b, b) of row g
+          const uint32_t s2b = sh * 0x10001u, b2b = bh * 0x10001u;  // row g+8
+          uint4 xlo[NT], xhi[NT];
 #pragma unroll
           for (int j = 0; j < NT; ++j) {
-            if (xok[j]) {
-              const uint4* qx = reinterpret_cast<const uint4*>(xb + xoff[j] + cl * 128);
-              xb0[j] = qx[0];
-              xb1[j] = qx[1];
-            } else {
-              xb0[j] = make_uint4(0, 0, 0, 0);
-              xb1[j] = make_uint4(0, 0, 0, 0);
-            }
+            const uint4* qx = reinterpret_cast<const uint4*>(xq + xoff[j] + q * 128);
+            xlo[j] = qx[0];
+            xhi[j] = qx[1];
           }
-          const uint32_t s2a = prmt(sa, sa, 0x1010u), b2a = prmt(sa, sa, 0x3232u);
-          const uint32_t s2b = prmt(sbv, sbv, 0x1010u), b2b = prmt(sbv, sbv, 0x3232u);
+          // code pair (sb, sb+4) of each word after >> 4 sb
+          uint32_t a[4][4];
 #pragma unroll
           for (int sb = 0; sb < 4; ++sb) {
-            uint32_t a[4];
-            a[0] = dequant2(wa.x >> (4 * sb), s2a, b2a);  // row g,   k 2t..2t+1
-            a[1] = dequant2(wc.x >> (4 * sb), s2b, b2b);  // row g+8
-            a[2] = dequant2(wa.y >> (4 * sb), s2a, b2a);  // row g,   k 2t+8..
-            a[3] = dequant2(wc.y >> (4 * sb), s2b, b2b);  // row g+8
+            a[sb][0] = dequant2(wa.x >> (4 * sb), s2a, b2a);  // row g,   k 2t..2t+1
+            a[sb][1] = dequant2(wc.x >> (4 * sb), s2b, b2b);  // row g+8
+            a[sb][2] = dequant2(wa.y >> (4 * sb), s2a, b2a);  // row g,   k 2t+8..
+            a[sb][3] = dequant2(wc.y >> (4 * sb), s2b, b2b);  // row g+8
+          }
+#pragma unroll
+          for (int sb = 0; sb < 4; ++sb)
 #pragma unroll
             for (int j = 0; j < NT; ++j) {
-              const uint4& qx = sb < 2 ? xb0[j] : xb1[j];
-              mma_bf16_16816(acc[j], a, (sb & 1) ? qx.z : qx.x, (sb & 1) ? qx.w : qx.y, acc[j]);
+              const uint4& qx = sb < 2 ? xlo[j] : xhi[j];
+              mma_bf16_16816(acc[j], a[sb], (sb & 1) ? qx.z : qx.x, (sb & 1) ? qx.w : qx.y, acc[j]);
             }
-          }
         }
       }
       __syncwarp();  // every lane has read the stage before it is refilled
