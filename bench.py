@@ -258,6 +258,44 @@ def run_gpu(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def profile_step(args):
+    """One warm-up graph step and one measured step of the 64-layer engine at
+    verify width --k (the workload of the ncu launch lists in profiles/)."""
+    import numpy as np
+    import torch
+    import iam_b200 as I
+    K = args.k
+    d = I.Dims.qwen35_27b(max_ctx=CTX + 4 * K + 64, max_rows=max(K, 32))
+    e = I.Engine(d)
+    e.init_synthetic(SEED)
+    e.state_init(SEED, CTX)
+    toks = torch.from_numpy(np.random.default_rng(0).integers(0, d.vocab, K).astype(np.int32)).cuda()
+    out = torch.zeros(K, dtype=torch.int32, device="cuda")
+    st = torch.cuda.Stream()
+    for i in range(2):
+        e.verify_device(toks.data_ptr(), K, CTX if i == 0 else -1, out.data_ptr(), st.cuda_stream)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_step": K, "launches_per_step": e.step_launches(K)}))
+    e.close()
+
+
+def profile_qmm(args):
+    """A few launches of one W4A16 matmul shape N,K,M (random codes) for ncu."""
+    import torch
+    import iam_b200 as I
+    N, K, M = (int(v) for v in args.profile_qmm.split(","))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = torch.randint(-2**31, 2**31 - 1, (N, K // 8), dtype=torch.int32, device="cuda", generator=g)
+    s = (torch.rand(N, K // 64, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    b = (-8 * s.float()).to(torch.bfloat16)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    for _ in range(4):
+        I.qmm_affine4(w.data_ptr(), s.data_ptr(), b.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_qmm": [N, K, M]}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -266,7 +304,13 @@ def main():
     ap.add_argument("--k", type=int, default=32)
     ap.add_argument("--impl", default="iam")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--profile-step", action="store_true", help="two graph steps at --k, for ncu launch lists")
+    ap.add_argument("--profile-qmm", default=None, help="N,K,M: a few launches of one matmul, for ncu")
     args = ap.parse_args()
+    if args.profile_step:
+        return profile_step(args)
+    if args.profile_qmm:
+        return profile_qmm(args)
     args.warmup = max(args.warmup, 1)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
