@@ -58,6 +58,22 @@ int iam_version(void);
 int iam_qmm_affine4(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
                     uint16_t* y, int M, int N, int K, int group_size, void* stream);
 
+/* The same matmul on the tensor cores (tcgen05, bf16 weights dequantized into
+ * tensor memory) over weights re-packed once into 128-row x 256-k blocks.
+ * No counterpart in the reference, whose qmm reads the MLX layout on every
+ * call; these three replace the same dispatchQMatmul / encodeQMM call when
+ * the caller can keep a packed copy.  The engine packs its own weights.
+ *   iam_qmm_packed_bytes: size of the packed form of an [N, K] matrix (0 for
+ *     invalid sizes);
+ *   iam_qmm_pack_affine4: w, s, b as for iam_qmm_affine4 -> packed (device
+ *     memory of that size, 16-byte aligned), stream-ordered;
+ *   iam_qmm_affine4_packed: y = x . W^T, any M >= 1 (passes of 32 tokens). */
+size_t iam_qmm_packed_bytes(int N, int K);
+int iam_qmm_pack_affine4(const uint32_t* w, const uint16_t* s, const uint16_t* b, void* packed, int N, int K,
+                         void* stream);
+int iam_qmm_affine4_packed(const void* packed, const uint16_t* x, uint16_t* y, int M, int N, int K,
+                           void* stream);
+
 /* rms_norm_bf16 (full_forward.swift:59-86), applied to each of `rows` rows. */
 int iam_rms_norm_bf16(const uint16_t* x, const uint16_t* weight, uint16_t* out, int rows, int dim,
                       float eps, void* stream);

@@ -64,10 +64,11 @@ struct TensorRec {
 };
 
 struct QW {
-  uint32_t* w = nullptr;
+  uint32_t* w = nullptr;  // MLX layout (as loaded)
   uint16_t* s = nullptr;
   uint16_t* b = nullptr;
-  int rows = 0, cols = 0;  // local output rows, local K
+  unsigned char* packed = nullptr;  // tile-packed copy the tensor-core matmul reads
+  int rows = 0, cols = 0;           // local output rows, local K
 };
 
 struct Layer {
@@ -76,6 +77,7 @@ struct Layer {
   uint16_t* in_norm = nullptr;
   uint16_t* post_norm = nullptr;
   QW gate, up, down;
+  unsigned char* gateup = nullptr;  // gate and up packed as SwiGLU pairs
   // GDN
   QW qkv, z, bproj, aproj, out;
   uint16_t* conv_w = nullptr;
@@ -119,6 +121,11 @@ struct EngineImpl {
   std::map<std::string, int> by_name;
   char* pool = nullptr;
   size_t pool_bytes = 0;
+  // Tile-packed weights (qmm.cuh), rebuilt from the pool whenever a 4-bit
+  // tensor was loaded or generated since the last pack.
+  char* ppool = nullptr;
+  size_t ppool_bytes = 0;
+  bool packed_dirty = true;
 
   std::vector<Layer> layers;
   uint16_t* embed = nullptr;
@@ -371,6 +378,31 @@ int alloc_all(EngineImpl& e) {
   e.final_norm = static_cast<uint16_t*>(tptr(e, "model.norm.weight"));
   e.lm = qw(e, "lm_head", e.vocab_l, H);
 
+  // packed copies: one pool, every matrix at a 256-byte boundary, zero padding
+  {
+    std::vector<std::pair<unsigned char**, size_t>> want;
+    auto need = [&](unsigned char** dst, int rows, int K, bool swiglu) {
+      want.push_back({dst, (qp_bytes(qp_tiles(rows, swiglu), K) + kAlign - 1) / kAlign * kAlign});
+    };
+    for (Layer& L : e.layers) {
+      need(&L.gateup, e.inter_l, H, true);
+      need(&L.down.packed, L.down.rows, L.down.cols, false);
+      for (QW* q : {&L.q, &L.k, &L.v, &L.o, &L.qkv, &L.z, &L.bproj, &L.aproj, &L.out})
+        if (q->w) need(&q->packed, q->rows, q->cols, false);
+    }
+    need(&e.lm.packed, e.lm.rows, e.lm.cols, false);
+    size_t tot = 0;
+    for (auto& w : want) tot += w.second;
+    E_CUDA(cudaMalloc(&e.ppool, std::max<size_t>(tot, 256)));
+    E_CUDA(cudaMemset(e.ppool, 0, std::max<size_t>(tot, 256)));
+    e.ppool_bytes = tot;
+    size_t off = 0;
+    for (auto& w : want) {
+      *w.first = reinterpret_cast<unsigned char*>(e.ppool + off);
+      off += w.second;
+    }
+  }
+
   // state
   const size_t s_per = static_cast<size_t>(e.gv_l) * d.gdn_dk * d.gdn_dv;
   E_CUDA(cudaMalloc(&e.S, std::max<size_t>(1, e.n_gdn * s_per) * sizeof(float)));
@@ -464,11 +496,29 @@ double qbytes(const QW& q) { return static_cast<double>(q.rows) * q.cols * (0.5 
 
 void seg_of(QmmSeg& s, const QW& q, int mode) {
   s = QmmSeg{};
+  s.packed = q.packed;
   s.w = q.w;
   s.s = q.s;
   s.b = q.b;
   s.rows = q.rows;
   s.mode = mode;
+}
+
+// Rebuilds the packed weights from the loaded ones (never during capture).
+int ensure_packed(EngineImpl& e) {
+  if (!e.packed_dirty) return IAM_OK;
+  auto pk = [&](const QW& q) { return qmm_pack(q.w, q.s, q.b, q.rows, q.cols, q.packed, 128, 0, e.stream); };
+  for (const Layer& L : e.layers) {
+    E_RUN(qmm_pack(L.gate.w, L.gate.s, L.gate.b, L.gate.rows, L.gate.cols, L.gateup, 64, 0, e.stream));
+    E_RUN(qmm_pack(L.up.w, L.up.s, L.up.b, L.up.rows, L.up.cols, L.gateup, 64, 64, e.stream));
+    E_RUN(pk(L.down));
+    for (const QW* q : {&L.q, &L.k, &L.v, &L.o, &L.qkv, &L.z, &L.bproj, &L.aproj, &L.out})
+      if (q->w) E_RUN(pk(*q));
+  }
+  E_RUN(pk(e.lm));
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  e.packed_dirty = false;
+  return IAM_OK;
 }
 
 int run_qmm(EngineImpl& e, QmmArgs& a, const char* kind, double bytes) {
@@ -615,6 +665,7 @@ int enqueue_mlp(EngineImpl& e, const Layer& L, int K) {
   a.K = H;
   a.nseg = 1;
   seg_of(a.seg[0], L.gate, EPI_SWIGLU);
+  a.seg[0].packed = L.gateup;
   a.seg[0].w2 = L.up.w;
   a.seg[0].s2 = L.up.s;
   a.seg[0].b2 = L.up.b;
@@ -695,11 +746,8 @@ int enqueue_step(EngineImpl& e, int K) {
   a.seg[0].key_ld = d.max_rows;
   a.seg[0].col_base = e.voff;
   E_RUN(run_qmm(e, a, "qmm", qbytes(e.lm)));
-  // number of lm_head CTAs of the plan (the key rows written)
-  QmmArgs probe = a;
-  probe.M = std::min(K, 32);
-  qmm_plan(probe);
-  const int nparts = probe.total_ctas;
+  // one key row per 128-row lm_head tile
+  const int nparts = qp_tiles(e.lm.rows, false);
   if (e.world == 1) {
     Recorder rec(e, "finalize", 8.0 * nparts * K);
     E_RUN(launch_finalize(e.keys, nparts, d.max_rows, K, e.d_in->tokens, e.d_out + 1, e.d_out, e.stream, e.pdl));
@@ -870,7 +918,7 @@ extern "C" void iam_destroy(iam_engine* eng) {
   for (auto& kv : e.graphs) cudaGraphExecDestroy(kv.second);
   e.graphs.clear();
   if (e.comm) iam::nccl_destroy(e.comm);
-  void* bufs[] = {e.pool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
+  void* bufs[] = {e.pool, e.ppool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
                   e.mid, e.mlp_h, e.q_buf, e.part_o, e.part_ml, e.red32, e.keys, e.best, e.rope_cs, e.d_in, e.d_out,
                   e.d_err, e.qws, e.qctr};
   for (void* p : bufs)
@@ -905,6 +953,7 @@ extern "C" int iam_load_tensor(iam_engine* eng, const char* name, const void* ho
     dst += nrows * width;
   }
   E_CUDA(cudaStreamSynchronize(e.stream));
+  if (t.kind == Kind::kQ4Words || t.kind == Kind::kQ4Scales || t.kind == Kind::kQ4Biases) e.packed_dirty = true;
   return IAM_OK;
 }
 
@@ -953,6 +1002,7 @@ extern "C" int iam_init_synthetic(iam_engine* eng, uint64_t seed) {
   E_CUDA(cudaSetDevice(e.device));
   for (const TensorRec& t : e.tensors) E_RUN(synth_tensor(e, t, seed));
   E_CUDA(cudaStreamSynchronize(e.stream));
+  e.packed_dirty = true;
   return IAM_OK;
 }
 
@@ -1047,6 +1097,8 @@ static int verify_common(iam_engine* eng, int K, int pos) {
   EngineImpl& e = eng->impl;
   IAM_CHECK(K >= 1 && K <= e.d.max_rows, "iam_verify: K out of range (1..max_rows)");
   IAM_CHECK(pos >= 0 && pos + K <= e.d.max_ctx, "iam_verify: pos + K exceeds max_ctx");
+  E_CUDA(cudaSetDevice(e.device));
+  E_RUN(ensure_packed(e));
   return IAM_OK;
 }
 
@@ -1116,6 +1168,7 @@ extern "C" int iam_step_launches(iam_engine* eng, int K) {
   if (!eng) return -1;
   EngineImpl& e = eng->impl;
   // count launches by enqueueing into a throw-away capture
+  if (cudaSetDevice(e.device) != cudaSuccess || iam::ensure_packed(e) != IAM_OK) return -1;
   cudaGraphExec_t g = nullptr;
   const int before = e.launches;
   if (e.graphs.count(K)) {

@@ -813,7 +813,7 @@ size_t qmm_ws_counters(const QmmArgs& a, const QmmConfig& c) {
 }
 
 namespace {
-// Split-K workspace of the operator-level entry point: library-owned, zeroed,
+// Split-K workspace of the operator-level entry points: library-owned, zeroed,
 // grown on demand, one per device.  (The engine passes its own.)
 struct OpWs {
   float* ws = nullptr;
@@ -822,7 +822,9 @@ struct OpWs {
 };
 OpWs g_opws[64];
 
-int op_workspace(size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** ctr) {
+}  // namespace
+
+int qmm_op_workspace(size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** ctr) {
   int dev = 0;
   IAM_CUDA(cudaGetDevice(&dev));
   IAM_CHECK(dev >= 0 && dev < 64, "qmm: device index out of range");
@@ -843,7 +845,6 @@ int op_workspace(size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** 
   *ctr = w.ctr;
   return IAM_OK;
 }
-}  // namespace
 
 // Validates one matmul and launches it in passes of at most 32 tokens.  A null
 // a.ws selects the library's own split-K workspace.
@@ -852,6 +853,28 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
   IAM_CHECK(a.M >= 1, "qmm: M must be >= 1");
   IAM_CHECK(a.nseg >= 1 && a.nseg <= kQmmMaxSeg, "qmm: 1..4 segments");
   IAM_CHECK(aligned16(a.x) && a.ldx % 8 == 0, "qmm: x must be 16-byte aligned with ldx % 8 == 0");
+  bool packed = a.seg[0].packed != nullptr;
+  for (int i = 1; i < a.nseg; ++i)
+    IAM_CHECK((a.seg[i].packed != nullptr) == packed, "qmm: segments mix packed and MLX-layout weights");
+  if (packed) {
+    const int total_m = a.M;
+    const uint16_t* x0 = a.x;
+    for (int m0 = 0; m0 < total_m; m0 += 32) {
+      QmmArgs p = a;
+      p.M = std::min(32, total_m - m0);
+      p.x = x0 + static_cast<size_t>(m0) * a.ldx;
+      for (int i = 0; i < p.nseg; ++i) {
+        QmmSeg& s = p.seg[i];
+        if (s.out) s.out += static_cast<size_t>(m0) * s.ldo;
+        if (s.out32) s.out32 += static_cast<size_t>(m0) * s.ldo;
+        if (s.resid) s.resid += static_cast<size_t>(m0) * s.ldr;
+        if (s.keys) s.keys += m0;
+      }
+      const int r = qmm_tc_run(p, st, pdl, ws_floats_cap, ws_ctr_cap);
+      if (r != IAM_OK) return r;
+    }
+    return IAM_OK;
+  }
   for (int i = 0; i < a.nseg; ++i) {
     const QmmSeg& s = a.seg[i];
     IAM_CHECK(s.rows > 0 && s.w && s.s && s.b, "qmm: segment without weights");
@@ -879,7 +902,7 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
     if (c.ks > 1) {
       const size_t nf = qmm_ws_floats(p, c), nc = qmm_ws_counters(p, c);
       if (!a.ws) {
-        const int r = op_workspace(nf, nc, st, &p.ws, &p.counters);
+        const int r = qmm_op_workspace(nf, nc, st, &p.ws, &p.counters);
         if (r != IAM_OK) return r;
       } else {
         IAM_CHECK(nf <= ws_floats_cap && nc <= ws_ctr_cap, "qmm: split-K workspace too small");

@@ -16,6 +16,7 @@ enum QmmEpi : int {
 };
 
 struct QmmSeg {
+  const unsigned char* packed;  // tile-packed weights (qmm_pack_*); used instead of w/s/b when set
   const uint32_t* w;   // [rows, K/8] MLX packing
   const uint16_t* s;   // [rows, K/64] bf16
   const uint16_t* b;   // [rows, K/64] bf16
@@ -83,6 +84,39 @@ inline int qmm_rows_per_cta(int mode, int rt) { return (mode == EPI_SWIGLU ? 8 :
 // Fills cta_begin of each segment and total_ctas; picks the config.
 QmmConfig qmm_plan(QmmArgs& a);
 int qmm_launch(const QmmArgs& a, const QmmConfig& c, cudaStream_t st, bool pdl);
+
+// ---- tile-packed weights for the tensor-core kernel (qmm_tc.cu)
+//
+// A matrix of `rows` x K becomes ceil(rows / 128) tiles (SwiGLU pairs: 64
+// features a tile, gate rows 0-63 and up rows 64-127) of ceil(K / 256)
+// blocks of kQpBlockBytes, tile-major:
+//   block (t, kb) at (t * KB + kb) * kQpBlockBytes;
+//   codes: row r at r * 128, its 32-k chunk c (4 words) at ((c ^ (r & 7)) * 16);
+//     each word holds 8 consecutive k with nibble s = k 2s, nibble s+4 = k 2s+1
+//     (so (w >> 4s) & 0x000F000F is the natural pair (k 2s, k 2s+1));
+//   (scale, bias) of row r, group g (0..3) at kQpCodeBytes + r * 16 + g * 4
+//     (scale in the low half).
+// Padding rows and k read as zero codes with zero scale and bias.
+constexpr int kQpRows = 128;
+constexpr int kQpBlockK = 256;
+constexpr int kQpCodeBytes = kQpRows * kQpBlockK / 2;   // 16384
+constexpr int kQpBlockBytes = kQpCodeBytes + kQpRows * 16;  // 18432
+inline int qp_kblocks(int K) { return (K + kQpBlockK - 1) / kQpBlockK; }
+inline size_t qp_bytes(int tiles, int K) { return static_cast<size_t>(tiles) * qp_kblocks(K) * kQpBlockBytes; }
+inline int qp_tiles(int rows, bool swiglu) { return (rows + (swiglu ? 63 : 127)) / (swiglu ? 64 : 128); }
+
+// Writes rows [0, rows) of an MLX matrix into packed tiles: source row r goes
+// to tile r / per_tile, tile row row_off + r % per_tile (per_tile 128 with
+// row_off 0, or 64 with row_off 0 / 64 for the gate / up half of SwiGLU
+// pairs).  Rows of the tiles it does not write keep their contents.
+int qmm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int rows, int K, unsigned char* dst,
+             int per_tile, int row_off, cudaStream_t st);
+
+// Tensor-core matmul over packed segments (every segment has `packed`; M <= 32).
+// A null a.ws selects the library's own split-K workspace.
+int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap);
+// The library's zeroed split-K workspace for operator-level calls (grown on demand).
+int qmm_op_workspace(size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** ctr);
 
 // Order-preserving key: larger float -> larger key; ties -> smaller index wins.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {

@@ -42,6 +42,50 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
   return false;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Contiguous global -> shared bulk copy (no multicast) completing on `bar`;
+// both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// As mbar_wait, but polls with relaxed semantics and orders the caller's later
+// accesses after the barrier with a lightweight acquire fence.  Cheaper per
+// poll (about 100 cycles instead of about 400), for threads whose issue rate
+// matters (a tensor-core issuer).
+__device__ __forceinline__ bool mbar_wait_light(uint32_t bar, uint32_t phase) {
+  for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.relaxed.cta.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(phase)
+        : "memory");
+    if (done) {
+      asm volatile("fence.acquire.sync_restrict::shared::cluster.cluster;" ::: "memory");
+      return true;
+    }
+  }
+  return false;
+}
+
+// Non-blocking: has the phase of parity `phase` completed?
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t phase) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(phase)
+      : "memory");
+  return done != 0;
+}
+
 // 2D tiled TMA load (no multicast) into shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
@@ -51,9 +95,11 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Encodes a 2D row-major tensor map [rows, cols] of `esize`-byte elements with
-// a [box_rows, box_cols] box.  Returns IAM_OK or IAM_EINVAL / IAM_ECUDA.
+// Encodes a 2D row-major tensor map [rows, cols] of `esize`-byte elements
+// (row pitch `pitch` elements, 0 = cols) with a [box_rows, box_cols] box.
+// Elements outside [rows, cols] read as zero.  Returns IAM_OK or IAM_EINVAL /
+// IAM_ECUDA.
 int tma_encode_2d(CUtensorMap* map, const void* base, int esize, uint64_t rows, uint64_t cols, uint32_t box_rows,
-                  uint32_t box_cols, bool swizzle128);
+                  uint32_t box_cols, bool swizzle128, uint64_t pitch = 0);
 
 }  // namespace iam

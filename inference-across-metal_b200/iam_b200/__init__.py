@@ -27,6 +27,9 @@ _SIGS = {
     "iam_status_string": (C.c_char_p, [_i]),
     "iam_version": (_i, []),
     "iam_qmm_affine4": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "iam_qmm_packed_bytes": (_sz, [_i, _i]),
+    "iam_qmm_pack_affine4": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    "iam_qmm_affine4_packed": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "iam_rms_norm_bf16": (_i, [_vp, _vp, _vp, _i, _i, _f, _vp]),
     "iam_silu_multiply_bf16": (_i, [_vp, _vp, _vp, _i, _vp]),
     "iam_residual_add_bf16": (_i, [_vp, _vp, _vp, _i, _vp]),
@@ -105,6 +108,18 @@ def _s(stream):
 # ------------------------------------------------------------ operator level
 def qmm_affine4(w, s, b, x, y, M, N, K, group_size=64, stream=None):
     _check(lib().iam_qmm_affine4(w, s, b, x, y, M, N, K, group_size, _s(stream)))
+
+
+def qmm_packed_bytes(N, K) -> int:
+    return int(lib().iam_qmm_packed_bytes(N, K))
+
+
+def qmm_pack_affine4(w, s, b, packed, N, K, stream=None):
+    _check(lib().iam_qmm_pack_affine4(w, s, b, packed, N, K, _s(stream)))
+
+
+def qmm_affine4_packed(packed, x, y, M, N, K, stream=None):
+    _check(lib().iam_qmm_affine4_packed(packed, x, y, M, N, K, _s(stream)))
 
 
 def rms_norm_bf16(x, weight, out, rows, dim, eps=1e-6, stream=None):

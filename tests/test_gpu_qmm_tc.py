@@ -1,0 +1,121 @@
+"""Tensor-core W4A16 matmul (tcgen05, weights dequantized into tensor memory)
+through the C ABI: the packed weight layout byte for byte against a numpy
+restatement, and the matmul against the oracle restatement of MLX's qmm.
+
+Tolerance as for iam_qmm_affine4: both sides multiply x with the bf16 weights
+bf16(q * scale + bias); only the fp32 accumulation order differs, so relative
+error <= 1e-2 and cosine >= 0.9999.
+"""
+import numpy as np
+import pytest
+
+from oracle import iam_oracle as O
+from oracle import synth
+
+from gpu_util import assert_close_bf16, dev, empty_u16, host_u16, ptr
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import iam_b200 as I  # noqa: E402
+
+u = O.to_u16
+
+ROWS, BLOCK_K, CODE_BYTES, BLOCK_BYTES = 128, 256, 16384, 18432
+
+
+def pack_ref(w, s, b):
+    """numpy restatement of the packed layout (qmm.cuh): tiles of 128 rows x
+    256 k, codes row-major with 16-byte chunks swizzled by (chunk ^ row % 8),
+    nibble s of a word = k 2s, nibble s+4 = k 2s+1; (scale | bias << 16) words
+    after the codes."""
+    N, KW = w.shape
+    K = KW * 8
+    KB = -(-K // BLOCK_K)
+    T = -(-N // ROWS)
+    out = np.zeros((T, KB, BLOCK_BYTES), np.uint8)
+    nib = (w[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 15  # [N, KW, 8] k order
+    perm = np.array([0, 2, 4, 6, 1, 3, 5, 7])  # stored nibble p holds k perm[p]
+    words = np.zeros((N, KB * 32), np.uint32)
+    words[:, :KW] = (nib[:, :, perm] << (4 * np.arange(8, dtype=np.uint32))).sum(axis=2, dtype=np.uint32)
+    G = K // 64
+    sb = np.zeros((N, KB * 4), np.uint32)
+    sb[:, :G] = s.view(np.uint16).astype(np.uint32) | (b.view(np.uint16).astype(np.uint32) << 16)
+    for r in range(N):
+        t, tr = divmod(r, ROWS)
+        for kb in range(KB):
+            blk = out[t, kb]
+            chunks = words[r, kb * 32:(kb + 1) * 32].reshape(8, 4)
+            for c in range(8):
+                o = tr * 128 + ((c ^ (tr & 7)) << 4)
+                blk[o:o + 16] = chunks[c].view(np.uint8)
+            blk[CODE_BYTES + tr * 16:CODE_BYTES + tr * 16 + 16] = sb[r, kb * 4:kb * 4 + 4].view(np.uint8)
+    return out.reshape(-1)
+
+
+def pack_dev(w, s, b, N, K):
+    nbytes = I.qmm_packed_bytes(N, K)
+    assert nbytes == -(-N // ROWS) * -(-K // BLOCK_K) * BLOCK_BYTES
+    packed = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    keep = [dev(w, torch), dev(s.view(np.uint16), torch), dev(b.view(np.uint16), torch)]
+    I.qmm_pack_affine4(*[ptr(t) for t in keep], ptr(packed), N, K)
+    torch.cuda.synchronize()
+    return packed
+
+
+def test_pack_layout_matches_restatement():
+    N, K = 200, 640  # a partial tile and a partial k block
+    w, s, b = synth.gen_qweight(21, "t.pack", N, K)
+    got = pack_dev(w, s, b, N, K).cpu().numpy()
+    assert np.array_equal(got, pack_ref(w, s, b))
+
+
+def _case(N, K, M, indep_bias=False, seed=31):
+    w, s, b = synth.gen_qweight(seed, f"t.tc.{N}x{K}", N, K)
+    if indep_bias:  # biases not tied to the scales
+        b = synth.gen_normal_bf16(seed + 1, f"t.tc.b.{N}x{K}", N * K // 64, 0.05).reshape(N, K // 64)
+    x = synth.gen_normal_bf16(seed + 2, f"t.tc.x.{M}x{K}", M * K, 1.0).astype(np.float32).reshape(M, K)
+    ref = O.qmm_affine4(x, w, s.astype(np.float32), b.astype(np.float32))
+    packed = pack_dev(w, s, b, N, K)
+    dx = dev(u(x), torch)
+    y = empty_u16(torch, M, N)
+    I.qmm_affine4_packed(ptr(packed), ptr(dx), ptr(y), M, N, K)
+    torch.cuda.synchronize()
+    return host_u16(y), ref
+
+
+@pytest.mark.parametrize("N,K", [(10240, 5120), (6144, 5120), (48, 5120), (5120, 6144), (1024, 5120)])
+@pytest.mark.parametrize("M", [1, 3, 8, 16, 17, 32, 40])
+def test_qmm_packed_matches_oracle(N, K, M):
+    got, ref = _case(N, K, M)
+    assert_close_bf16(got, ref)
+
+
+@pytest.mark.parametrize("N,K,M", [(5120, 17408, 4), (5120, 17408, 32), (264, 704, 5), (128, 256, 1)])
+def test_qmm_packed_odd_shapes(N, K, M):
+    got, ref = _case(N, K, M, indep_bias=True, seed=41)
+    assert_close_bf16(got, ref)
+
+
+def test_qmm_packed_repeat_is_deterministic():
+    """Split-K partials meet in a workspace the last CTA re-zeroes: a second
+    call must give the same bits."""
+    w, s, b = synth.gen_qweight(51, "t.tc.rep", 1024, 6144)
+    x = synth.gen_normal_bf16(52, "t.tc.rep.x", 32 * 6144, 1.0).reshape(32, 6144)
+    packed = pack_dev(w, s, b, 1024, 6144)
+    dx = dev(x.view(np.uint16), torch)
+    ys = []
+    for _ in range(2):
+        y = empty_u16(torch, 32, 1024)
+        I.qmm_affine4_packed(ptr(packed), ptr(dx), ptr(y), 32, 1024, 6144)
+        torch.cuda.synchronize()
+        ys.append(host_u16(y))
+    assert np.array_equal(ys[0], ys[1])
+
+
+def test_qmm_packed_rejects_bad_shapes():
+    assert I.qmm_packed_bytes(16, 100) == 0
+    with pytest.raises(I.IamError):
+        I.qmm_affine4_packed(0, 0, 0, 1, 16, 64)
+    with pytest.raises(I.IamError):
+        I.qmm_pack_affine4(0, 0, 0, 0, 16, 96)
