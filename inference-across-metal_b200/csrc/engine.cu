@@ -507,10 +507,20 @@ void seg_of(QmmSeg& s, const QW& q, int mode) {
 // Rebuilds the packed weights from the loaded ones (never during capture).
 int ensure_packed(EngineImpl& e) {
   if (!e.packed_dirty) return IAM_OK;
-  auto pk = [&](const QW& q) { return qmm_pack(q.w, q.s, q.b, q.rows, q.cols, q.packed, 128, 0, e.stream); };
+  auto pk = [&](const QW& q) {
+    const int tiles = qp_tiles(q.rows, false);
+    int r = qmm_pack_begin(q.packed, tiles, q.cols, e.stream);
+    if (r == IAM_OK) r = qmm_pack_scan(q.s, q.rows, q.cols, q.packed, tiles, 128, e.stream);
+    if (r == IAM_OK) r = qmm_pack(q.w, q.s, q.b, q.rows, q.cols, q.packed, tiles, 128, 0, e.stream);
+    return r;
+  };
   for (const Layer& L : e.layers) {
-    E_RUN(qmm_pack(L.gate.w, L.gate.s, L.gate.b, L.gate.rows, L.gate.cols, L.gateup, 64, 0, e.stream));
-    E_RUN(qmm_pack(L.up.w, L.up.s, L.up.b, L.up.rows, L.up.cols, L.gateup, 64, 64, e.stream));
+    const int gt = qp_tiles(e.inter_l, true);
+    E_RUN(qmm_pack_begin(L.gateup, gt, L.gate.cols, e.stream));
+    E_RUN(qmm_pack_scan(L.gate.s, L.gate.rows, L.gate.cols, L.gateup, gt, 64, e.stream));
+    E_RUN(qmm_pack_scan(L.up.s, L.up.rows, L.up.cols, L.gateup, gt, 64, e.stream));
+    E_RUN(qmm_pack(L.gate.w, L.gate.s, L.gate.b, L.gate.rows, L.gate.cols, L.gateup, gt, 64, 0, e.stream));
+    E_RUN(qmm_pack(L.up.w, L.up.s, L.up.b, L.up.rows, L.up.cols, L.gateup, gt, 64, 64, e.stream));
     E_RUN(pk(L.down));
     for (const QW* q : {&L.q, &L.k, &L.v, &L.o, &L.qkv, &L.z, &L.bproj, &L.aproj, &L.out})
       if (q->w) E_RUN(pk(*q));

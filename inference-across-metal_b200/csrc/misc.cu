@@ -26,14 +26,22 @@ __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restric
   if (tid < 32) {
     float p[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const int nj = dim / 256;
-    for (int j = 0; j < nj; ++j) {
-      const uint4 v = *reinterpret_cast<const uint4*>(xr + 256 * j + 8 * tid);
-      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    // loads issued eight at a time (one latency per eight), summed in j order
+    for (int j0 = 0; j0 < nj; j0 += 8) {
+      uint4 v[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float a0 = lo_bf(u[i]), a1 = hi_bf(u[i]);
-        p[2 * i] += a0 * a0;
-        p[2 * i + 1] += a1 * a1;
+      for (int k = 0; k < 8; ++k)
+        if (j0 + k < nj) v[k] = *reinterpret_cast<const uint4*>(xr + 256 * (j0 + k) + 8 * tid);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (j0 + k >= nj) break;
+        const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float a0 = lo_bf(u[i]), a1 = hi_bf(u[i]);
+          p[2 * i] += a0 * a0;
+          p[2 * i + 1] += a1 * a1;
+        }
       }
     }
 #pragma unroll

@@ -95,22 +95,36 @@ int qmm_launch(const QmmArgs& a, const QmmConfig& c, cudaStream_t st, bool pdl);
 //     each word holds 8 consecutive k with nibble s = k 2s, nibble s+4 = k 2s+1
 //     (so (w >> 4s) & 0x000F000F is the natural pair (k 2s, k 2s+1));
 //   (scale, bias) of row r, group g (0..3) at kQpCodeBytes + r * 16 + g * 4
-//     (scale in the low half).
+//     (scale in the low half);
+// then one byte a tile: 1 when every scale of the tile is below 0.25 in
+// magnitude, in which case the tile's scales are stored multiplied by 2^130
+// (exact: a power of two, and the product stays below the bf16 maximum).
+// Such tiles are converted with the code as a bf16 subnormal q * 2^-130 and
+// one packed FMA, fma(q * 2^-130, s * 2^130, b) = bf16(q * s + b) with one
+// rounding -- the same bits as the general form, one instruction fewer a pair.
 // Padding rows and k read as zero codes with zero scale and bias.
 constexpr int kQpRows = 128;
 constexpr int kQpBlockK = 256;
 constexpr int kQpCodeBytes = kQpRows * kQpBlockK / 2;   // 16384
 constexpr int kQpBlockBytes = kQpCodeBytes + kQpRows * 16;  // 18432
 inline int qp_kblocks(int K) { return (K + kQpBlockK - 1) / kQpBlockK; }
-inline size_t qp_bytes(int tiles, int K) { return static_cast<size_t>(tiles) * qp_kblocks(K) * kQpBlockBytes; }
+inline size_t qp_blocks_bytes(int tiles, int K) {
+  return static_cast<size_t>(tiles) * qp_kblocks(K) * kQpBlockBytes;
+}
+inline size_t qp_bytes(int tiles, int K) { return qp_blocks_bytes(tiles, K) + (static_cast<size_t>(tiles) + 255) / 256 * 256; }
 inline int qp_tiles(int rows, bool swiglu) { return (rows + (swiglu ? 63 : 127)) / (swiglu ? 64 : 128); }
 
-// Writes rows [0, rows) of an MLX matrix into packed tiles: source row r goes
-// to tile r / per_tile, tile row row_off + r % per_tile (per_tile 128 with
-// row_off 0, or 64 with row_off 0 / 64 for the gate / up half of SwiGLU
-// pairs).  Rows of the tiles it does not write keep their contents.
+// Packing, in three stream-ordered steps per packed matrix `dst` of `tiles`
+// tiles: qmm_pack_begin sets every tile flag; qmm_pack_scan clears the flag
+// of each tile holding a scale >= 0.25 in magnitude (or not finite) among
+// the rows of one source; qmm_pack then writes the rows of one source.  A
+// source's row r goes to tile r / per_tile, tile row row_off + r % per_tile
+// (per_tile 128 with row_off 0, or 64 with row_off 0 / 64 for the gate / up
+// half of SwiGLU pairs).  Scan every source of the matrix before packing any.
+int qmm_pack_begin(unsigned char* dst, int tiles, int K, cudaStream_t st);
+int qmm_pack_scan(const uint16_t* s, int rows, int K, unsigned char* dst, int tiles, int per_tile, cudaStream_t st);
 int qmm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int rows, int K, unsigned char* dst,
-             int per_tile, int row_off, cudaStream_t st);
+             int tiles, int per_tile, int row_off, cudaStream_t st);
 
 // Tensor-core matmul over packed segments (every segment has `packed`; M <= 32).
 // A null a.ws selects the library's own split-K workspace.

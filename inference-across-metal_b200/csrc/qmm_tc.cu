@@ -81,11 +81,42 @@ __device__ __forceinline__ void dequant_group(const uint4& c0, const uint4& c1, 
     for (int s = 0; s < 4; ++s) r[4 * j + s] = dequant2(w[j] >> (4 * s), s2, b2);
 }
 
+// The same for a tile whose scales were stored times 2^130: the code moved to
+// bits 3-6 of each half is the bf16 subnormal q * 2^-130, and one packed FMA
+// gives bf16(q * scale + bias) with the product exact and one rounding.
+__device__ __forceinline__ void dequant_group_fast(const uint4& c0, const uint4& c1, uint32_t sb, uint32_t (&r)[32]) {
+  const uint32_t s2 = prmt(sb, sb, 0x1010u), b2 = prmt(sb, sb, 0x3232u);
+  const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const uint32_t v = s == 0 ? (w[j] << 3) : (w[j] >> (4 * s - 3));
+      r[4 * j + s] = fma_bf2(v & 0x00780078u, s2, b2);
+    }
+}
+
 __device__ __forceinline__ float4 ld_cg_f4(const float* p) {
   float4 r;
   asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(p));
   return r;
 }
+
+// Cursor over an N-stage ring: stage index and the parity of its current lap
+// (no divisions in the hot loops).
+template <int N>
+struct Ring {
+  int idx = 0;
+  uint32_t phase = 0;
+  bool first_lap = true;
+  __device__ __forceinline__ void next() {
+    if (++idx == N) {
+      idx = 0;
+      phase ^= 1u;
+      first_lap = false;
+    }
+  }
+};
 
 struct QmmTcArgs {
   CUtensorMap xmap;  // x [M, K] bf16, box [NN tokens x 64 k], 128B swizzle
@@ -236,10 +267,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     constexpr uint32_t idesc = umma_idesc_bf16(128, NN);
     const uint32_t dt = tmem + kTcDCol;
     bool ok = true;
-    for (int i = 0; i < nkb; ++i) {
-      const int slot = i % kTcASlots, xsl = i % XS;
-      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(xfull(xsl), (i / XS) & 1) &&
-                                       mbar_wait_light(afull(slot), (i / kTcASlots) & 1))) {
+    Ring<kTcASlots> ar;
+    Ring<XS> xr;
+    for (int i = 0; i < nkb; ++i, ar.next(), xr.next()) {
+      const int slot = ar.idx, xsl = xr.idx;
+      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(xfull(xsl), xr.phase, abort_flag) &&
+                                       mbar_wait_light(afull(slot), ar.phase, abort_flag))) {
         ok = false;
         break;
       }
@@ -267,10 +300,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     const int q = warp & 3, h = (warp - 2) >> 2;  // h: 64-k group of each block
     const int row = 32 * q + lane;
     const uint32_t lane_base = tmem + ((32u * q) << 16);
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % WS;
+    const bool sw = S.mode == EPI_SWIGLU;
+    const int seg_tiles = (S.rows + (sw ? 63 : 127)) / (sw ? 64 : 128);
+    const bool fast = S.packed[static_cast<size_t>(seg_tiles) * KB * kQpBlockBytes + tile] != 0;
+    Ring<WS> wr;
+    Ring<kTcASlots> ar;
+    for (int i = 0; i < nkb; ++i, wr.next(), ar.next()) {
+      const int s = wr.idx;
       // every branch below is warp-uniform: tcgen05.st/ld need the whole warp
-      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(wfull(s), (i / WS) & 1))) {
+      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(wfull(s), wr.phase, abort_flag))) {
         give_up();
         break;
       }
@@ -280,15 +318,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
       const uint32_t sb = *reinterpret_cast<const uint32_t*>(blk + kQpCodeBytes + row * 16 + h * 4);
       __syncwarp();
       if (lane == 0) mbar_arrive(wempty(s));
-      const int slot = i % kTcASlots, n = i / kTcASlots;
-      if (!__all_sync(0xffffffffu, n == 0 || mbar_wait_light(aempty(slot), (n - 1) & 1))) {
+      const int slot = ar.idx;
+      if (!__all_sync(0xffffffffu, ar.first_lap || mbar_wait_light(aempty(slot), ar.phase ^ 1u, abort_flag))) {
         give_up();
         break;
       }
       tc_fence_after();
       uint32_t r[32];
-      dequant_group(c0, c1, sb, r);
-      tmem_st32(lane_base + slot * 128 + h * 32, r);
+      if (fast) {
+        dequant_group_fast(c0, c1, sb, r);
+      } else {
+        dequant_group(c0, c1, sb, r);
+      }
+      tmem_st8x4(lane_base + slot * 128 + h * 32, r);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -424,10 +466,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------- packing
+// Clears the flag of every tile holding a scale that is not below 0.25 in
+// magnitude (bf16 exponent field >= 125, non-finite values included).
+__global__ void qmm_pack_scan_kernel(const uint16_t* __restrict__ s, int rows, int G, unsigned char* __restrict__ flags,
+                                     int per_tile) {
+  const long long total = static_cast<long long>(rows) * G;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    if (((s[idx] >> 7) & 0xFF) >= 125) flags[(idx / G) / per_tile] = 0;
+  }
+}
+
 // One thread per (tile, k block, row): 8 chunks of codes and 4 (scale, bias) pairs.
 __global__ void qmm_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ s,
                                 const uint16_t* __restrict__ b, int rows, int K, unsigned char* __restrict__ dst,
-                                int per_tile, int row_off) {
+                                const unsigned char* __restrict__ flags, int per_tile, int row_off) {
   const int KB = (K + kQpBlockK - 1) / kQpBlockK;
   const int G = K / 64, KW = K / 8;
   const long long total = static_cast<long long>(rows) * KB;
@@ -451,12 +504,18 @@ __global__ void qmm_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* 
       }
       *reinterpret_cast<uint4*>(blk + tr * 128 + ((c ^ (tr & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
+    const bool fast = flags[t] != 0;
     uint32_t sbv[4];
     for (int g = 0; g < 4; ++g) {
       const int gg = kb * 4 + g;
-      sbv[g] = gg < G ? (static_cast<uint32_t>(s[static_cast<size_t>(r) * G + gg]) |
-                         (static_cast<uint32_t>(b[static_cast<size_t>(r) * G + gg]) << 16))
-                      : 0u;
+      uint32_t sc = 0, bi = 0;
+      if (gg < G) {
+        sc = s[static_cast<size_t>(r) * G + gg];
+        bi = b[static_cast<size_t>(r) * G + gg];
+        // exact: |scale| < 0.25, so scale * 2^130 is a finite bf16 with the same digits
+        if (fast) sc = f2bf(ldexpf(bf2f(static_cast<uint16_t>(sc)), 130));
+      }
+      sbv[g] = sc | (bi << 16);
     }
     *reinterpret_cast<uint4*>(blk + kQpCodeBytes + tr * 16) = make_uint4(sbv[0], sbv[1], sbv[2], sbv[3]);
   }
@@ -511,16 +570,36 @@ int tc_plan_ks(int tiles, int KB, int occ) {
 
 }  // namespace
 
+int qmm_pack_begin(unsigned char* dst, int tiles, int K, cudaStream_t st) {
+  IAM_CHECK(dst && tiles > 0 && K > 0, "qmm_pack_begin: bad arguments");
+  IAM_CUDA(cudaMemsetAsync(dst + qp_blocks_bytes(tiles, K), 1, static_cast<size_t>(tiles), st));
+  return IAM_OK;
+}
+
+int qmm_pack_scan(const uint16_t* s, int rows, int K, unsigned char* dst, int tiles, int per_tile, cudaStream_t st) {
+  IAM_CHECK(s && dst && rows > 0 && K > 0 && K % 64 == 0 && (per_tile == 128 || per_tile == 64),
+            "qmm_pack_scan: bad arguments");
+  IAM_CHECK((rows + per_tile - 1) / per_tile <= tiles, "qmm_pack_scan: rows exceed the packed tiles");
+  const long long total = static_cast<long long>(rows) * (K / 64);
+  const int threads = 256;
+  const int blocks = static_cast<int>(std::min<long long>((total + threads - 1) / threads, 148LL * 32));
+  qmm_pack_scan_kernel<<<blocks, threads, 0, st>>>(s, rows, K / 64, dst + qp_blocks_bytes(tiles, K), per_tile);
+  IAM_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
 int qmm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int rows, int K, unsigned char* dst,
-             int per_tile, int row_off, cudaStream_t st) {
+             int tiles, int per_tile, int row_off, cudaStream_t st) {
   IAM_CHECK(w && s && b && dst && rows > 0 && K > 0 && K % 64 == 0, "qmm_pack: bad arguments");
   IAM_CHECK((per_tile == 128 && row_off == 0) || (per_tile == 64 && (row_off == 0 || row_off == 64)),
             "qmm_pack: bad tile split");
+  IAM_CHECK((rows + per_tile - 1) / per_tile <= tiles, "qmm_pack: rows exceed the packed tiles");
   IAM_CHECK(aligned16(dst), "qmm_pack: destination must be 16-byte aligned");
   const long long total = static_cast<long long>(rows) * qp_kblocks(K);
   const int threads = 128;
   const int blocks = static_cast<int>(std::min<long long>((total + threads - 1) / threads, 148LL * 64));
-  qmm_pack_kernel<<<blocks, threads, 0, st>>>(w, s, b, rows, K, dst, per_tile, row_off);
+  qmm_pack_kernel<<<blocks, threads, 0, st>>>(w, s, b, rows, K, dst, dst + qp_blocks_bytes(tiles, K), per_tile,
+                                              row_off);
   IAM_CUDA(cudaGetLastError());
   return IAM_OK;
 }
@@ -606,8 +685,13 @@ extern "C" int iam_qmm_pack_affine4(const uint32_t* w, const uint16_t* s, const 
   IAM_CHECK(N > 0 && K > 0 && K % 64 == 0, "iam_qmm_pack_affine4: N > 0 and K a positive multiple of 64");
   IAM_CHECK(w && s && b && packed, "iam_qmm_pack_affine4: null pointer");
   const cudaStream_t st = as_stream(stream);
-  IAM_CUDA(cudaMemsetAsync(packed, 0, qp_bytes(qp_tiles(N, false), K), st));
-  return qmm_pack(w, s, b, N, K, static_cast<unsigned char*>(packed), 128, 0, st);
+  const int tiles = qp_tiles(N, false);
+  unsigned char* dst = static_cast<unsigned char*>(packed);
+  IAM_CUDA(cudaMemsetAsync(packed, 0, qp_bytes(tiles, K), st));
+  int r = qmm_pack_begin(dst, tiles, K, st);
+  if (r == IAM_OK) r = qmm_pack_scan(s, N, K, dst, tiles, 128, st);
+  if (r == IAM_OK) r = qmm_pack(w, s, b, N, K, dst, tiles, 128, 0, st);
+  return r;
 }
 
 extern "C" int iam_qmm_affine4_packed(const void* packed, const uint16_t* x, uint16_t* y, int M, int N, int K,

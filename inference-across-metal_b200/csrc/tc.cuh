@@ -35,6 +35,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// 32 columns as four 8-column stores (8-register operand groups are easier
+// on the register allocator than one 32-register group).
+__device__ __forceinline__ void tmem_st8x4(uint32_t taddr, const uint32_t (&r)[32]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr + 8 * c),
+                 "r"(r[8 * c]), "r"(r[8 * c + 1]), "r"(r[8 * c + 2]), "r"(r[8 * c + 3]), "r"(r[8 * c + 4]),
+                 "r"(r[8 * c + 5]), "r"(r[8 * c + 6]), "r"(r[8 * c + 7])
+                 : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {

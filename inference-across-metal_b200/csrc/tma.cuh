@@ -28,8 +28,12 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// Returns false when the phase did not complete within the poll budget.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
+// Returns false when the phase did not complete within the poll budget, or
+// (when `abort` is given) once another thread of the CTA has raised *abort:
+// after one wait gave up, the others end promptly instead of each spending
+// its own budget.  Waits for copies or MMAs already in flight pass no abort
+// flag -- those complete by themselves and must before the CTA exits.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase, const volatile int* abort = nullptr) {
   for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
     uint32_t done;
     asm volatile(
@@ -38,6 +42,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
         : "r"(bar), "r"(phase)
         : "memory");
     if (done) return true;
+    if (abort && (i & 63) == 63 && *abort) return false;
   }
   return false;
 }
@@ -58,7 +63,7 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 // accesses after the barrier with a lightweight acquire fence.  Cheaper per
 // poll (about 100 cycles instead of about 400), for threads whose issue rate
 // matters (a tensor-core issuer).
-__device__ __forceinline__ bool mbar_wait_light(uint32_t bar, uint32_t phase) {
+__device__ __forceinline__ bool mbar_wait_light(uint32_t bar, uint32_t phase, const volatile int* abort = nullptr) {
   for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
     uint32_t done;
     asm volatile(
@@ -71,6 +76,7 @@ __device__ __forceinline__ bool mbar_wait_light(uint32_t bar, uint32_t phase) {
       asm volatile("fence.acquire.sync_restrict::shared::cluster.cluster;" ::: "memory");
       return true;
     }
+    if (abort && (i & 63) == 63 && *abort) return false;
   }
   return false;
 }

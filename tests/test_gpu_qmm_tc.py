@@ -28,7 +28,9 @@ def pack_ref(w, s, b):
     """numpy restatement of the packed layout (qmm.cuh): tiles of 128 rows x
     256 k, codes row-major with 16-byte chunks swizzled by (chunk ^ row % 8),
     nibble s of a word = k 2s, nibble s+4 = k 2s+1; (scale | bias << 16) words
-    after the codes."""
+    after the codes; then one flag byte a tile (padded to 256 bytes): 1 when
+    every scale of the tile is below 0.25 in magnitude, and then the tile's
+    scales are stored times 2^130."""
     N, KW = w.shape
     K = KW * 8
     KB = -(-K // BLOCK_K)
@@ -39,8 +41,16 @@ def pack_ref(w, s, b):
     words = np.zeros((N, KB * 32), np.uint32)
     words[:, :KW] = (nib[:, :, perm] << (4 * np.arange(8, dtype=np.uint32))).sum(axis=2, dtype=np.uint32)
     G = K // 64
+    s16 = s.view(np.uint16)
+    flags = np.ones(T, np.uint8)
+    for t in range(T):
+        if np.any(((s16[t * ROWS:(t + 1) * ROWS] >> 7) & 0xFF) >= 125):
+            flags[t] = 0
+    # 2^130 overflows float32 on its own; the products (|s| < 0.25) do not
+    s_big = (s.astype(np.float64) * 2.0 ** 130).astype(np.float32).astype(synth.BF16).view(np.uint16)
+    s_st = np.where(np.repeat(flags, ROWS)[:N, None] == 1, s_big, s16)
     sb = np.zeros((N, KB * 4), np.uint32)
-    sb[:, :G] = s.view(np.uint16).astype(np.uint32) | (b.view(np.uint16).astype(np.uint32) << 16)
+    sb[:, :G] = s_st.astype(np.uint32) | (b.view(np.uint16).astype(np.uint32) << 16)
     for r in range(N):
         t, tr = divmod(r, ROWS)
         for kb in range(KB):
@@ -50,12 +60,14 @@ def pack_ref(w, s, b):
                 o = tr * 128 + ((c ^ (tr & 7)) << 4)
                 blk[o:o + 16] = chunks[c].view(np.uint8)
             blk[CODE_BYTES + tr * 16:CODE_BYTES + tr * 16 + 16] = sb[r, kb * 4:kb * 4 + 4].view(np.uint8)
-    return out.reshape(-1)
+    tail = np.zeros(-(-T // 256) * 256, np.uint8)
+    tail[:T] = flags
+    return np.concatenate([out.reshape(-1), tail])
 
 
 def pack_dev(w, s, b, N, K):
     nbytes = I.qmm_packed_bytes(N, K)
-    assert nbytes == -(-N // ROWS) * -(-K // BLOCK_K) * BLOCK_BYTES
+    assert nbytes == -(-N // ROWS) * -(-K // BLOCK_K) * BLOCK_BYTES + -(-(-(-N // ROWS)) // 256) * 256
     packed = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     keep = [dev(w, torch), dev(s.view(np.uint16), torch), dev(b.view(np.uint16), torch)]
     I.qmm_pack_affine4(*[ptr(t) for t in keep], ptr(packed), N, K)
@@ -63,11 +75,45 @@ def pack_dev(w, s, b, N, K):
     return packed
 
 
+def big_scales(s, rows):
+    """Scales of `rows` raised to 0.3 in one group each: those tiles take the
+    general conversion (no 2^130 pre-scaling)."""
+    s = s.copy()
+    s[rows, 1] = synth.BF16(0.3)
+    return s
+
+
 def test_pack_layout_matches_restatement():
     N, K = 200, 640  # a partial tile and a partial k block
     w, s, b = synth.gen_qweight(21, "t.pack", N, K)
     got = pack_dev(w, s, b, N, K).cpu().numpy()
-    assert np.array_equal(got, pack_ref(w, s, b))
+    ref = pack_ref(w, s, b)
+    assert ref[-256] == 1  # small scales: the fast conversion
+    assert np.array_equal(got, ref)
+    s2 = big_scales(s, [150])  # second tile only
+    got = pack_dev(w, s2, b, N, K).cpu().numpy()
+    ref = pack_ref(w, s2, b)
+    assert ref[-256] == 1 and ref[-255] == 0
+    assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("M", [1, 32])
+def test_qmm_packed_mixed_tiles(M):
+    """Tiles with a scale >= 0.25 use the general conversion, the others the
+    2^130 pre-scaled one; both must match the oracle."""
+    N, K = 512, 1024
+    w, s, b = synth.gen_qweight(61, "t.tc.mixed", N, K)
+    s = big_scales(s, [5, 300])  # tiles 0 and 2
+    x = synth.gen_normal_bf16(62, f"t.tc.mixed.x.{M}", M * K, 1.0).astype(np.float32).reshape(M, K)
+    ref = O.qmm_affine4(x, w, s.astype(np.float32), b.astype(np.float32))
+    packed = pack_dev(w, s, b, N, K)
+    flags = packed.cpu().numpy()[-256:-252]
+    assert list(flags) == [0, 1, 0, 1]
+    dx = dev(u(x), torch)
+    y = empty_u16(torch, M, N)
+    I.qmm_affine4_packed(ptr(packed), ptr(dx), ptr(y), M, N, K)
+    torch.cuda.synchronize()
+    assert_close_bf16(host_u16(y), ref)
 
 
 def _case(N, K, M, indep_bias=False, seed=31):
