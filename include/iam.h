@@ -11,7 +11,8 @@
  * Two levels, mirroring the reference (inference-across-metal):
  *  - operator level: one call per reference kernel, on caller-owned device
  *    buffers (the reference's Metal argument slots, full_forward.swift:55-445,
- *    711-728); nothing is allocated;
+ *    711-728); the only device memory the library allocates at this level is
+ *    its own split-K and attention scratch, grown on demand;
  *  - engine level: weights, recurrent state and KV cache owned by the library
  *    and resident in HBM, a whole token step captured as one CUDA graph
  *    (replaces forwardPass, full_forward.swift:1198-1308, and the M-row

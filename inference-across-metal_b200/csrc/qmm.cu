@@ -820,15 +820,19 @@ struct OpWs {
   int* ctr = nullptr;
   size_t floats = 0, ctrs = 0;
 };
-OpWs g_opws[64];
+// [device][kind]: the mma.sync kernels sum partials into a workspace they keep
+// zeroed; the tensor-core kernel stores partials without clearing them, so the
+// two never share one.
+OpWs g_opws[64][2];
 
 }  // namespace
 
-int qmm_op_workspace(size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** ctr) {
+int qmm_op_workspace(int kind, size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** ctr) {
   int dev = 0;
   IAM_CUDA(cudaGetDevice(&dev));
   IAM_CHECK(dev >= 0 && dev < 64, "qmm: device index out of range");
-  OpWs& w = g_opws[dev];
+  IAM_CHECK(kind == 0 || kind == 1, "qmm: workspace kind");
+  OpWs& w = g_opws[dev][kind];
   if (w.floats < floats || w.ctrs < ctrs) {
     IAM_CUDA(cudaStreamSynchronize(st));
     cudaFree(w.ws);
@@ -902,7 +906,7 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
     if (c.ks > 1) {
       const size_t nf = qmm_ws_floats(p, c), nc = qmm_ws_counters(p, c);
       if (!a.ws) {
-        const int r = qmm_op_workspace(nf, nc, st, &p.ws, &p.counters);
+        const int r = qmm_op_workspace(0, nf, nc, st, &p.ws, &p.counters);
         if (r != IAM_OK) return r;
       } else {
         IAM_CHECK(nf <= ws_floats_cap && nc <= ws_ctr_cap, "qmm: split-K workspace too small");
@@ -937,3 +941,4 @@ extern "C" int iam_qmm_affine4(const uint32_t* w, const uint16_t* s, const uint1
   a.seg[0].mode = EPI_STORE;
   return qmm_run(a, as_stream(stream), false);
 }
+

@@ -129,8 +129,10 @@ int qmm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int rows, 
 // Tensor-core matmul over packed segments (every segment has `packed`; M <= 32).
 // A null a.ws selects the library's own split-K workspace.
 int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap);
-// The library's zeroed split-K workspace for operator-level calls (grown on demand).
-int qmm_op_workspace(size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** ctr);
+// The library's split-K workspace for operator-level calls (grown on demand,
+// zeroed when grown): kind 0 for the mma.sync kernels (which keep it zero),
+// kind 1 for the tensor-core kernel (which keeps only its counters zero).
+int qmm_op_workspace(int kind, size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** ctr);
 
 // Order-preserving key: larger float -> larger key; ties -> smaller index wins.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {

@@ -656,7 +656,7 @@ int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_
   if (ks > 1) {
     const size_t nf = static_cast<size_t>(cta) * ks * kQpRows * NN, nc = static_cast<size_t>(cta);
     if (!a.ws) {
-      const int r = qmm_op_workspace(nf, nc, st, &a.ws, &a.counters);
+      const int r = qmm_op_workspace(1, nf, nc, st, &a.ws, &a.counters);
       if (r != IAM_OK) return r;
     } else {
       IAM_CHECK(nf <= ws_floats_cap && nc <= ws_ctr_cap, "qmm: split-K workspace too small");

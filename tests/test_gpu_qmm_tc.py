@@ -165,3 +165,19 @@ def test_qmm_packed_rejects_bad_shapes():
         I.qmm_affine4_packed(0, 0, 0, 1, 16, 64)
     with pytest.raises(I.IamError):
         I.qmm_pack_affine4(0, 0, 0, 0, 16, 96)
+
+
+def test_mma_sync_qmm_after_tensor_core_split_k():
+    """The tensor-core kernel leaves fp32 partials in its split-K workspace;
+    the mma.sync kernel's operator-level workspace must stay zero regardless:
+    a split-K tensor-core call followed by a split-K iam_qmm_affine4 call."""
+    _case(1024, 6144, 32)  # tensor core, K split over CTAs
+    N, K, M = 1024, 5120, 8
+    w, s, b = synth.gen_qweight(81, "t.tc.then.sync", N, K)
+    x = synth.gen_normal_bf16(82, "t.tc.then.sync.x", M * K, 1.0).astype(np.float32).reshape(M, K)
+    ref = O.qmm_affine4(x, w, s.astype(np.float32), b.astype(np.float32))
+    keep = [dev(w, torch), dev(s.view(np.uint16), torch), dev(b.view(np.uint16), torch), dev(u(x), torch)]
+    y = empty_u16(torch, M, N)
+    I.qmm_affine4(*[ptr(t) for t in keep], ptr(y), M, N, K)
+    torch.cuda.synchronize()
+    assert_close_bf16(host_u16(y), ref)
