@@ -12,7 +12,8 @@
  *  - operator level: one call per reference kernel, on caller-owned device
  *    buffers (the reference's Metal argument slots, full_forward.swift:55-445,
  *    711-728); the only device memory the library allocates at this level is
- *    its own split-K and attention scratch, grown on demand;
+ *    its own split-K and attention scratch, grown on demand (see
+ *    iam_qmm_affine4_noalloc for a variant that allocates nothing);
  *  - engine level: weights, recurrent state and KV cache owned by the library
  *    and resident in HBM, a whole token step captured as one CUDA graph
  *    (replaces forwardPass, full_forward.swift:1198-1308, and the M-row
@@ -58,6 +59,20 @@ int iam_version(void);
  * affine_qmm_t_nax_bfloat16_t_gs_64_b_4 kernel with args (w,s,b,x,y,K,N,M). */
 int iam_qmm_affine4(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
                     uint16_t* y, int M, int N, int K, int group_size, void* stream);
+
+/* iam_qmm_affine4 for callers that cannot allocate device memory while they
+ * run it (they manage all device memory themselves, or run inside a section
+ * where an allocation would synchronise the device).  No counterpart in the
+ * reference.  Same arguments, kernel and results; the split-K scratch is a
+ * fixed array inside the library (1 Mi floats, 16 Ki counters) instead of a
+ * workspace grown on demand, and a shape whose plan needs more is rejected
+ * with IAM_EINVAL.  The first call on a device looks the scratch up
+ * (cudaGetSymbolAddress) and clears it (cudaMemset, synchronous); make it
+ * outside any stream capture.  The scratch is
+ * shared by all calls on a device: calls must not overlap (one stream, or
+ * ordered), and a call that failed part-way may leave it dirty. */
+int iam_qmm_affine4_noalloc(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
+                            uint16_t* y, int M, int N, int K, int group_size, void* stream);
 
 /* The same matmul on the tensor cores (tcgen05, bf16 weights dequantized into
  * tensor memory) over weights re-packed once into 128-row x 256-k blocks.

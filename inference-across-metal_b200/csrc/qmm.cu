@@ -942,3 +942,78 @@ extern "C" int iam_qmm_affine4(const uint32_t* w, const uint16_t* s, const uint1
   return qmm_run(a, as_stream(stream), false);
 }
 
+// ---------------------------------------------------------------- fixed scratch
+// A variant of iam_qmm_affine4 for callers that cannot allocate device memory
+// while they run it: a caller that manages all device memory itself (its own
+// pool, nothing left to hand to cudaMalloc), or one inside a section where an
+// allocation would synchronise the device or fail.  The split-K scratch is a
+// fixed array inside the library image instead of the library's grown-on-demand
+// workspace.
+namespace iam {
+namespace {
+constexpr size_t kNoAllocFloats = static_cast<size_t>(1) << 20;  // 4 MiB of fp32 partial sums
+constexpr size_t kNoAllocCounters = 16384;                        // one arrival counter a row block
+// Both must be zero when a call starts: the first call on a device clears them
+// and every call that completes leaves them zero again (the last CTA of a row
+// block clears what it summed).
+__device__ __align__(256) float g_noalloc_ws[kNoAllocFloats];
+__device__ __align__(256) int g_noalloc_ctr[kNoAllocCounters];
+struct NoAllocScratch {
+  float* ws = nullptr;
+  int* ctr = nullptr;
+};
+NoAllocScratch g_noalloc[64];  // device addresses, looked up once per device
+}  // namespace
+}  // namespace iam
+
+extern "C" int iam_qmm_affine4_noalloc(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
+                                       uint16_t* y, int M, int N, int K, int group_size, void* stream) {
+  using namespace iam;
+  IAM_CHECK(group_size == 64, "iam_qmm_affine4_noalloc: group_size must be 64");
+  IAM_CHECK(N > 0 && N % 8 == 0, "iam_qmm_affine4_noalloc: N must be a positive multiple of 8");
+  IAM_CHECK(M >= 1 && K > 0 && K % 64 == 0, "iam_qmm_affine4_noalloc: M >= 1 and K a positive multiple of 64");
+  IAM_CHECK(w && s && b && x && y, "iam_qmm_affine4_noalloc: null pointer");
+  int dev = 0;
+  IAM_CUDA(cudaGetDevice(&dev));
+  IAM_CHECK(dev >= 0 && dev < 64, "iam_qmm_affine4_noalloc: device index out of range");
+  NoAllocScratch& sc = g_noalloc[dev];
+  if (!sc.ws) {  // first call on this device: a lookup and a clear, no allocation
+    float* ws = nullptr;
+    int* ctr = nullptr;
+    IAM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&ws), g_noalloc_ws));
+    IAM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&ctr), g_noalloc_ctr));
+    IAM_CUDA(cudaMemset(ws, 0, kNoAllocFloats * sizeof(float)));
+    IAM_CUDA(cudaMemset(ctr, 0, kNoAllocCounters * sizeof(int)));
+    sc.ws = ws;
+    sc.ctr = ctr;
+  }
+  QmmArgs a = {};
+  a.x = x;
+  a.ldx = K;
+  a.M = M;
+  a.K = K;
+  a.nseg = 1;
+  a.seg[0].w = w;
+  a.seg[0].s = s;
+  a.seg[0].b = b;
+  a.seg[0].out = y;
+  a.seg[0].ldo = N;
+  a.seg[0].rows = N;
+  a.seg[0].mode = EPI_STORE;
+  // the passes are of 32 tokens and a remainder: check both plans' scratch
+  for (int pm : {std::min(M, 32), M % 32}) {
+    if (pm == 0) continue;
+    QmmArgs probe = a;
+    probe.M = pm;
+    const QmmConfig c = qmm_plan(probe);
+    if (c.ks < 2) continue;
+    const size_t nf = qmm_ws_floats(probe, c), nc = qmm_ws_counters(probe, c);
+    if (nf > kNoAllocFloats || nc > kNoAllocCounters)
+      return fail(IAM_EINVAL, "iam_qmm_affine4_noalloc: this shape needs " + std::to_string(nf) + " floats and " +
+                                  std::to_string(nc) + " counters of split-K scratch; the fixed scratch holds " +
+                                  std::to_string(kNoAllocFloats) + " and " + std::to_string(kNoAllocCounters));
+  }
+  a.ws = sc.ws;
+  a.counters = sc.ctr;
+  return qmm_run(a, as_stream(stream), false, kNoAllocFloats, kNoAllocCounters);
+}

@@ -27,6 +27,7 @@ _SIGS = {
     "iam_status_string": (C.c_char_p, [_i]),
     "iam_version": (_i, []),
     "iam_qmm_affine4": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "iam_qmm_affine4_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "iam_qmm_packed_bytes": (_sz, [_i, _i]),
     "iam_qmm_pack_affine4": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "iam_qmm_affine4_packed": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
@@ -108,6 +109,10 @@ def _s(stream):
 # ------------------------------------------------------------ operator level
 def qmm_affine4(w, s, b, x, y, M, N, K, group_size=64, stream=None):
     _check(lib().iam_qmm_affine4(w, s, b, x, y, M, N, K, group_size, _s(stream)))
+
+
+def qmm_affine4_noalloc(w, s, b, x, y, M, N, K, group_size=64, stream=None):
+    _check(lib().iam_qmm_affine4_noalloc(w, s, b, x, y, M, N, K, group_size, _s(stream)))
 
 
 def qmm_packed_bytes(N, K) -> int:
