@@ -31,6 +31,9 @@ sys.path.insert(0, os.path.join(ROOT, "inference-across-metal_b200"))
 SEED = 20261201
 CTX = 1024
 METRIC = "verified tokens/sec, Qwen3.5-27B-shape 4-bit at K=1/32, and % of HBM roofline"
+# dram__bytes_read.sum + dram__bytes_write.sum of one qmm_tc_kernel launch
+# (34816 x 5120 weights, 32 tokens) over its weight bytes (104.09 MB / 100.27 MB)
+TRAFFIC_PER_WEIGHT_BYTE = 104.090624 / 100.270080
 WORKLOAD = "qwen3.5-27b-shape 64-layer (48 GDN + 16 attn) 4-bit verify, ctx 1024, batch 1"
 
 
@@ -241,9 +244,13 @@ def run_gpu(args, rank, world, local_rank):
         "k1": {"value": 1000.0 / ms1, "unit": "tokens/s", "ms_per_step": ms1},
         "hbm_roofline_step": {"bytes_per_step_per_gpu": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": hbm,
                               "frac": step_gbs / hbm, "peak_kind": peak_kind},
-        "roofline": {"bound": "hbm", "kernel": "qmm_w4a16_kernel", "achieved": q_gbs, "peak": hbm, "unit": "GB/s",
-                     "frac": q_gbs / hbm, "traffic": None, "peak_kind": peak_kind,
-                     "launches_per_step": q["launches"], "ms_per_step": q["ms"]},
+        "roofline": {"bound": "hbm", "kernel": "qmm_tc_kernel", "achieved": q_gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": q_gbs / hbm,
+                     "traffic": TRAFFIC_PER_WEIGHT_BYTE * q["bytes"] / max(q["launches"], 1),
+                     "traffic_note": "DRAM read+write per average launch, scaled from the ncu capture in "
+                                     "profiles/qmm_tc_34816x5120_m32.md by weight bytes",
+                     "peak_kind": peak_kind, "launches_per_step": q["launches"], "ms_per_step": q["ms"],
+                     "timing": "eager step, CUDA events on the engine stream around each launch"},
         "kernels_ms": {k: round(v["ms"], 4) for k, v in prof.items()},
         "kernels_ms_k1": {k: round(v["ms"], 4) for k, v in prof1.items()},
         "e2e": {"value": K / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * (K + 1),
@@ -280,7 +287,8 @@ def profile_step(args):
 
 
 def profile_qmm(args):
-    """A few launches of one W4A16 matmul shape N,K,M (random codes) for ncu."""
+    """A few launches of one W4A16 matmul shape N,K,M (random codes, packed as
+    the engine packs them) through the tensor-core kernel, for ncu."""
     import torch
     import iam_b200 as I
     N, K, M = (int(v) for v in args.profile_qmm.split(","))
@@ -290,8 +298,10 @@ def profile_qmm(args):
     b = (-8 * s.float()).to(torch.bfloat16)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    pk = torch.empty(I.qmm_packed_bytes(N, K), dtype=torch.uint8, device="cuda")
+    I.qmm_pack_affine4(w.data_ptr(), s.data_ptr(), b.data_ptr(), pk.data_ptr(), N, K)
     for _ in range(4):
-        I.qmm_affine4(w.data_ptr(), s.data_ptr(), b.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K)
+        I.qmm_affine4_packed(pk.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K)
     torch.cuda.synchronize()
     print(json.dumps({"profile_qmm": [N, K, M]}))
 
