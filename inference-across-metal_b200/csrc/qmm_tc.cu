@@ -116,6 +116,20 @@ struct Ring {
       first_lap = false;
     }
   }
+  // positioned at element i, stepping two elements at a time (N > 2)
+  __device__ __forceinline__ void start(int i) {
+    idx = i % N;
+    phase = static_cast<uint32_t>(i / N) & 1u;
+    first_lap = i < N;
+  }
+  __device__ __forceinline__ void next2() {
+    idx += 2;
+    if (idx >= N) {
+      idx -= N;
+      phase ^= 1u;
+      first_lap = false;
+    }
+  }
 };
 
 struct QmmTcArgs {
@@ -177,14 +191,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
   if (threadIdx.x == 0) {
     for (int s = 0; s < WS; ++s) {
       mbar_init(wfull(s), 1);
-      mbar_init(wempty(s), kTcDqWarps);
+      mbar_init(wempty(s), kTcDqWarps / 2);  // the team that converts the block
     }
     for (int s = 0; s < XS; ++s) {
       mbar_init(xfull(s), 1);
       mbar_init(xempty(s), 1);
     }
     for (int s = 0; s < kTcASlots; ++s) {
-      mbar_init(afull(s), kTcDqWarps);
+      mbar_init(afull(s), kTcDqWarps / 2);
       mbar_init(aempty(s), 1);
     }
     mbar_init(dfull, 1);
@@ -303,9 +317,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     const bool sw = S.mode == EPI_SWIGLU;
     const int seg_tiles = (S.rows + (sw ? 63 : 127)) / (sw ? 64 : 128);
     const bool fast = S.packed[static_cast<size_t>(seg_tiles) * KB * kQpBlockBytes + tile] != 0;
+    // Two teams of eight warps take alternate blocks; a warp converts two
+    // 64-k groups (gp: groups 2gp, 2gp+1) of its quadrant's rows per visit.
+    // The teams drift apart by half a block, so one team's barrier waits and
+    // store latencies overlap the other team's conversion on every SM
+    // sub-partition.
+    const int team = (warp - 2) >> 3, gp = ((warp - 2) >> 2) & 1;
     Ring<WS> wr;
     Ring<kTcASlots> ar;
-    for (int i = 0; i < nkb; ++i, wr.next(), ar.next()) {
+    wr.start(team);
+    ar.start(team);
+    for (int i = team; i < nkb; i += 2, wr.next2(), ar.next2()) {
       const int s = wr.idx;
       // every branch below is warp-uniform: tcgen05.st/ld need the whole warp
       if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(wfull(s), wr.phase, abort_flag))) {
@@ -313,9 +335,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         break;
       }
       const unsigned char* blk = smem + L::kWOff + s * kQpBlockBytes;
-      const uint4 c0 = *reinterpret_cast<const uint4*>(blk + row * 128 + (((2 * h) ^ (row & 7)) << 4));
-      const uint4 c1 = *reinterpret_cast<const uint4*>(blk + row * 128 + (((2 * h + 1) ^ (row & 7)) << 4));
-      const uint32_t sb = *reinterpret_cast<const uint32_t*>(blk + kQpCodeBytes + row * 16 + h * 4);
+      uint4 c[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        c[j] = *reinterpret_cast<const uint4*>(blk + row * 128 + (((4 * gp + j) ^ (row & 7)) << 4));
+      const uint2 sb = *reinterpret_cast<const uint2*>(blk + kQpCodeBytes + row * 16 + gp * 8);
       __syncwarp();
       if (lane == 0) mbar_arrive(wempty(s));
       const int slot = ar.idx;
@@ -326,11 +350,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
       tc_fence_after();
       uint32_t r[32];
       if (fast) {
-        dequant_group_fast(c0, c1, sb, r);
+        dequant_group_fast(c[0], c[1], sb.x, r);
       } else {
-        dequant_group(c0, c1, sb, r);
+        dequant_group(c[0], c[1], sb.x, r);
       }
-      tmem_st8x4(lane_base + slot * 128 + h * 32, r);
+      tmem_st8x4(lane_base + slot * 128 + (2 * gp) * 32, r);
+      if (fast) {
+        dequant_group_fast(c[2], c[3], sb.y, r);
+      } else {
+        dequant_group(c[2], c[3], sb.y, r);
+      }
+      tmem_st8x4(lane_base + slot * 128 + (2 * gp + 1) * 32, r);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
