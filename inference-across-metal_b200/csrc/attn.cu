@@ -13,6 +13,7 @@
 #include <cmath>
 
 #include "kernels.cuh"
+#include "tma.cuh"
 
 namespace iam {
 namespace {
@@ -191,6 +192,202 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- decode on tensor cores
+// The same split-context decode for wide verify blocks, on mma.sync
+// m16n8k16 (bf16 in, fp32 accumulate).  The (token, query head) pairs of a KV
+// head form the rows of a small attention problem; one CTA takes 64 of them
+// (four warps of 16) against the 64-key chunks of its context split:
+// S = Q K^T and O += P V run on the tensor cores from padded shared memory
+// (ldmatrix), the online softmax in registers; P is rounded to bf16 for the
+// P V product, the row sums l use the unrounded p.  Partials go to the same
+// (max, sum, o) slots as attn_decode_kernel and attn_combine_kernel merges them.
+constexpr int kTcPairs = 64;              // query (token, head) rows a CTA
+constexpr int kTcKeys = 64;               // keys a staged chunk
+constexpr int kTcStride = kHeadDim + 8;   // padded smem row: ldmatrix without bank conflicts
+constexpr size_t kTcSmem = static_cast<size_t>(3) * 64 * kTcStride * 2;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(128, 1) attn_decode_tc_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint16_t* sq = reinterpret_cast<uint16_t*>(smem_raw);
+  uint16_t* sk = sq + kTcPairs * kTcStride;
+  uint16_t* sv = sk + kTcKeys * kTcStride;
+  pdl_wait();
+  pdl_trigger();
+  const int split = blockIdx.x, kvh = blockIdx.y, p0 = blockIdx.z * kTcPairs;
+  const int rep = a.n_heads / a.n_kv_heads;
+  const int npairs = a.rows * rep;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int pos0 = cur_pos(a);
+  const int t_hi = (min(p0 + kTcPairs, npairs) - 1) / rep;
+  const int nkeys = min(pos0 + t_hi, a.max_ctx - 1) + 1;
+  const int nch = (nkeys + kTcKeys - 1) / kTcKeys;
+  const int c_begin = static_cast<int>((static_cast<long long>(split) * nch) / a.nsplit);
+  const int c_end = static_cast<int>((static_cast<long long>(split + 1) * nch) / a.nsplit);
+  // this lane's two rows (pairs) and their query positions (-1: no such row)
+  const int r_lo = warp * 16 + g, r_hi = r_lo + 8;
+  const int pl = p0 + r_lo, ph = p0 + r_hi;
+  const int qpos_lo = pl < npairs ? min(pos0 + pl / rep, a.max_ctx - 1) : -1;
+  const int qpos_hi = ph < npairs ? min(pos0 + ph / rep, a.max_ctx - 1) : -1;
+  auto part_of = [&](int p) {
+    const int t = p / rep, h = kvh * rep + p % rep;
+    return (static_cast<size_t>(t) * a.n_heads + h) * a.nsplit + split;
+  };
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  float o[32][4];
+#pragma unroll
+  for (int nd = 0; nd < 32; ++nd)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[nd][e] = 0.f;
+
+  if (c_begin < c_end) {
+    for (int i = threadIdx.x; i < kTcPairs * (kHeadDim / 8); i += blockDim.x) {
+      const int r = i / (kHeadDim / 8), d8 = (i % (kHeadDim / 8)) * 8;
+      const int p = p0 + r;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (p < npairs) {
+        const int t = p / rep, h = kvh * rep + p % rep;
+        v = *reinterpret_cast<const uint4*>(a.q_buf + (static_cast<size_t>(t) * a.n_heads + h) * kHeadDim + d8);
+      }
+      *reinterpret_cast<uint4*>(sq + r * kTcStride + d8) = v;
+    }
+    const uint32_t sq_a = smem_addr(sq), sk_a = smem_addr(sk), sv_a = smem_addr(sv);
+    const int lr = lane & 7, lj = lane >> 3;  // ldmatrix: row in matrix, matrix index
+    for (int c = c_begin; c < c_end; ++c) {
+      const int kbase = c * kTcKeys;
+      __syncthreads();  // previous chunk consumed (and q staged on the first pass)
+      for (int i = threadIdx.x; i < kTcKeys * (kHeadDim / 8); i += blockDim.x) {
+        const int r = i / (kHeadDim / 8), d8 = (i % (kHeadDim / 8)) * 8;
+        uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+        if (kbase + r < nkeys) {
+          const size_t off = (static_cast<size_t>(kbase + r) * a.n_kv_heads + kvh) * kHeadDim + d8;
+          kk = *reinterpret_cast<const uint4*>(a.k_cache + off);
+          vv = *reinterpret_cast<const uint4*>(a.v_cache + off);
+        }
+        *reinterpret_cast<uint4*>(sk + r * kTcStride + d8) = kk;
+        *reinterpret_cast<uint4*>(sv + r * kTcStride + d8) = vv;
+      }
+      __syncthreads();
+      // S = Q K^T for the warp's 16 rows x 64 keys
+      float sc[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] = 0.f;
+#pragma unroll 4
+      for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+        uint32_t af[4];
+        ldsm_x4(sq_a + 2 * ((warp * 16 + (lj & 1) * 8 + lr) * kTcStride + 16 * kk + (lj >> 1) * 8), af);
+#pragma unroll
+        for (int n2 = 0; n2 < 4; ++n2) {
+          uint32_t bf[4];
+          ldsm_x4(sk_a + 2 * ((16 * n2 + (lj >> 1) * 8 + lr) * kTcStride + 16 * kk + (lj & 1) * 8), bf);
+          mma16816(sc[2 * n2], af, bf[0], bf[1]);
+          mma16816(sc[2 * n2 + 1], af, bf[2], bf[3]);
+        }
+      }
+      // scale, causal mask, online softmax (a row lives in the 4 lanes of a quad)
+      float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = kbase + nt * 8 + 2 * tq + (e & 1);
+          const int qp = e < 2 ? qpos_lo : qpos_hi;
+          const float v = key <= qp ? sc[nt][e] * 0.0625f : -INFINITY;  // 1/sqrt(256)
+          sc[nt][e] = v;
+          if (e < 2) mx_lo = fmaxf(mx_lo, v);
+          else mx_hi = fmaxf(mx_hi, v);
+        }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
+        mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
+      }
+      const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+      const float keep_lo = m_lo == -INFINITY ? 0.f : expf(m_lo - mn_lo);
+      const float keep_hi = m_hi == -INFINITY ? 0.f : expf(m_hi - mn_hi);
+      float sum_lo = 0.f, sum_hi = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mref = e < 2 ? mn_lo : mn_hi;
+          const float p = sc[nt][e] == -INFINITY ? 0.f : expf(sc[nt][e] - mref);
+          sc[nt][e] = p;
+          if (e < 2) sum_lo += p;
+          else sum_hi += p;
+        }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        sum_lo += __shfl_xor_sync(0xffffffffu, sum_lo, off);
+        sum_hi += __shfl_xor_sync(0xffffffffu, sum_hi, off);
+      }
+      l_lo = l_lo * keep_lo + sum_lo;
+      l_hi = l_hi * keep_hi + sum_hi;
+      m_lo = mn_lo;
+      m_hi = mn_hi;
+#pragma unroll
+      for (int nd = 0; nd < 32; ++nd) {
+        o[nd][0] *= keep_lo;
+        o[nd][1] *= keep_lo;
+        o[nd][2] *= keep_hi;
+        o[nd][3] *= keep_hi;
+      }
+      // O += P V: P (16 x 64, bf16) straight from the score registers
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t pa[4];
+        pa[0] = pack_bf2(sc[2 * ks][0], sc[2 * ks][1]);
+        pa[1] = pack_bf2(sc[2 * ks][2], sc[2 * ks][3]);
+        pa[2] = pack_bf2(sc[2 * ks + 1][0], sc[2 * ks + 1][1]);
+        pa[3] = pack_bf2(sc[2 * ks + 1][2], sc[2 * ks + 1][3]);
+#pragma unroll
+        for (int nd2 = 0; nd2 < 16; ++nd2) {
+          uint32_t bf[4];
+          ldsm_x4_t(sv_a + 2 * ((16 * ks + (lj & 1) * 8 + lr) * kTcStride + 16 * nd2 + (lj >> 1) * 8), bf);
+          mma16816(o[2 * nd2], pa, bf[0], bf[1]);
+          mma16816(o[2 * nd2 + 1], pa, bf[2], bf[3]);
+        }
+      }
+    }
+  }
+  // partials: (max, sum) and the unnormalised output of each of the lane's rows
+#pragma unroll
+  for (int hl = 0; hl < 2; ++hl) {
+    const int p = hl == 0 ? pl : ph;
+    if (p >= npairs) continue;
+    const size_t part = part_of(p);
+    if (c_begin < c_end) {
+      float* po = a.part_o + part * kHeadDim + 2 * tq;
+#pragma unroll
+      for (int nd = 0; nd < 32; ++nd)
+        *reinterpret_cast<float2*>(po + nd * 8) = make_float2(o[nd][2 * hl], o[nd][2 * hl + 1]);
+    }
+    if (tq == 0) {
+      a.part_ml[2 * part] = hl == 0 ? m_lo : m_hi;  // -inf when the split saw no key of this row
+      a.part_ml[2 * part + 1] = hl == 0 ? l_lo : l_hi;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- combine + gate
 __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
   pdl_wait();
@@ -274,16 +471,26 @@ int launch_attn_prep(const AttnArgs& a, cudaStream_t st, bool pdl) {
 int attn_init_attrs() {
   if (!g_attn_attr) {
     IAM_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(DecodeSmem)));
+    IAM_CUDA(cudaFuncSetAttribute(attn_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(kTcSmem)));
     g_attn_attr = true;
   }
   return IAM_OK;
 }
+
+// Verify blocks with at least kTcMinPairs (token, query head) pairs per KV
+// head take the tensor-core decode; narrower ones the warp-per-pair kernel.
+constexpr int kTcMinPairs = 32;
 
 int launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   IAM_CHECK(a.n_heads % a.n_kv_heads == 0 && a.n_heads / a.n_kv_heads <= 8, "attention: GQA group of at most 8");
   const int r = attn_init_attrs();
   if (r != IAM_OK) return r;
   IAM_CHECK(a.nsplit >= 1 && a.nsplit <= 64, "attention: 1..64 context splits");
+  const int npairs = a.rows * (a.n_heads / a.n_kv_heads);
+  if (npairs >= kTcMinPairs)
+    return launch_k(attn_decode_tc_kernel, dim3(a.nsplit, a.n_kv_heads, (npairs + kTcPairs - 1) / kTcPairs),
+                    dim3(128), kTcSmem, st, pdl, a);
   return launch_k(attn_decode_kernel, dim3(a.nsplit, a.n_kv_heads, (a.rows + kRowBlock - 1) / kRowBlock), dim3(256),
                   sizeof(DecodeSmem), st, pdl, a);
 }
