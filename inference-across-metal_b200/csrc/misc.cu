@@ -10,38 +10,35 @@ namespace iam {
 // rms_norm_bf16 (full_forward.swift:59-86), bit-exact with the reference's
 // summation order: the reference's thread i (of 256) sums x[i + 256 j] in j
 // order, then a shared-memory tree adds thread i + s into i for s = 128..1.
-// Here warp 0 plays all 256 threads: lane l owns virtual threads 8l..8l+7 and
-// reads them with one 16-byte load per j; tree levels s >= 8 are lane
-// shuffles (xor 16..1), s = 4, 2, 1 are in-lane.  rms = sqrt(sum / dim + eps);
-// then the whole CTA writes out = bf16((x / rms) * w) with 16-byte accesses.
+// Here the CTA stages the row in shared memory with one round of 16-byte
+// loads; warp 0 plays all 256 threads: lane l owns virtual threads
+// 8l..8l+7; tree levels s >= 8 are lane shuffles (xor 16..1), s = 4, 2, 1 are
+// in-lane.  rms = sqrt(sum / dim + eps); then the whole CTA writes
+// out = bf16((x / rms) * w) with 16-byte accesses.
 // Requires dim % 256 == 0.
 __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restrict__ x, int ldx,
                                                        const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
                                                        int ldo, int dim, float eps) {
+  extern __shared__ __align__(16) uint4 xs[];  // the row, staged in one round of loads
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
-  const uint16_t* xr = x + static_cast<size_t>(row) * ldx;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ldx);
+  const int nv = dim / 8;
+  for (int i = tid; i < nv; i += blockDim.x) xs[i] = xr[i];
+  __syncthreads();
   __shared__ float rms_s;
   if (tid < 32) {
     float p[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const int nj = dim / 256;
-    // loads issued eight at a time (one latency per eight), summed in j order
-    for (int j0 = 0; j0 < nj; j0 += 8) {
-      uint4 v[8];
+    for (int j = 0; j < nj; ++j) {
+      const uint4 v = xs[32 * j + tid];  // virtual threads 8 tid .. 8 tid + 7, element block j
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (j0 + k < nj) v[k] = *reinterpret_cast<const uint4*>(xr + 256 * (j0 + k) + 8 * tid);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (j0 + k >= nj) break;
-        const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float a0 = lo_bf(u[i]), a1 = hi_bf(u[i]);
-          p[2 * i] += a0 * a0;
-          p[2 * i + 1] += a1 * a1;
-        }
+      for (int i = 0; i < 4; ++i) {
+        const float a0 = lo_bf(u[i]), a1 = hi_bf(u[i]);
+        p[2 * i] += a0 * a0;
+        p[2 * i + 1] += a1 * a1;
       }
     }
 #pragma unroll
@@ -63,8 +60,8 @@ __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restric
   __syncthreads();
   const float rms = rms_s;
   uint16_t* orow = out + static_cast<size_t>(row) * ldo;
-  for (int i = tid; i < dim / 8; i += blockDim.x) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xr + 8 * i);
+  for (int i = tid; i < nv; i += blockDim.x) {
+    const uint4 v = xs[i];
     const uint4 ww = *reinterpret_cast<const uint4*>(w + 8 * i);
     const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, wv[4] = {ww.x, ww.y, ww.z, ww.w};
     uint32_t o[4];
@@ -77,11 +74,11 @@ __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restric
 
 int launch_rms_norm(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out, int ldo, int rows, int dim,
                     float eps, cudaStream_t st, bool pdl) {
-  IAM_CHECK(dim % 256 == 0, "rms_norm: dim must be a multiple of 256");
+  IAM_CHECK(dim % 256 == 0 && dim <= 16384, "rms_norm: dim must be a multiple of 256, at most 16384");
   IAM_CHECK(aligned16(x) && aligned16(w) && aligned16(out) && ldx % 8 == 0 && ldo % 8 == 0,
             "rms_norm: 16-byte aligned rows required");
-  return launch_k(rms_norm_kernel, dim3(rows), dim3(std::min(512, std::max(32, dim / 8))), 0, st, pdl, x, ldx, w, out,
-                  ldo, dim, eps);
+  return launch_k(rms_norm_kernel, dim3(rows), dim3(std::min(512, std::max(32, dim / 8))),
+                  static_cast<size_t>(dim) * 2, st, pdl, x, ldx, w, out, ldo, dim, eps);
 }
 
 // ---------------------------------------------------------------- element-wise

@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     // ------------------------------------------------------------ epilogue
     constexpr int EC = NN / 4;  // accumulator columns (tokens) per warp
     float v[EC];
-    const bool have = __all_sync(0xffffffffu, mbar_wait(dfull, 0));
+    const bool have = __all_sync(0xffffffffu, mbar_wait_light(dfull, 0));
     if (!have) give_up();
     tc_fence_after();
     if constexpr (EC == 8) {
@@ -395,18 +395,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         for (int c4 = 0; c4 < EC / 4; ++c4)
           *reinterpret_cast<float4*>(mine + 4 * c4) = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
       }
-      __threadfence();
+      // The barrier orders every thread's partial before one GPU-scope
+      // acquire-release arrival (cumulative, so it publishes the whole CTA's
+      // partial and, for the last arrival, acquires the others').
       named_bar_sync(1, 32 * kTcDqWarps);
       if (threadIdx.x == 64) {
         int* ctr = A.counters + bx;
-        const int l = atomicAdd(ctr, 1) == KS - 1;
+        int prev;
+        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
+        const int l = prev == KS - 1;
         if (l) *ctr = 0;
         *last_flag = l;
       }
       named_bar_sync(1, 32 * kTcDqWarps);
       last = *last_flag != 0;
       if (last) {
-        __threadfence();
 #pragma unroll
         for (int e = 0; e < EC; ++e) v[e] = 0.f;
         for (int j = 0; j < KS; ++j) {
