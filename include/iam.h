@@ -213,6 +213,29 @@ typedef struct iam_dims {
 /* Qwen3.5-27B defaults (full_forward.swift:18-49). */
 void iam_dims_qwen35_27b(iam_dims* d);
 
+/* The tensor-parallel shard that rank `rank` of `world` holds; host only, no
+ * GPU needed.  No counterpart in the reference (it runs on one device); the
+ * engine builds its tensor list from exactly this plan.  Each pair is
+ * [first, first + count) in the unsharded numbering:
+ *   GDN        V heads split evenly; the K heads they read follow them;
+ *   attention  query heads split evenly; KV heads split up to n_kv_heads
+ *              ways and are replicated beyond (rank r then holds KV head
+ *              r / (world / n_kv_heads));
+ *   MLP        intermediate columns (gate/up rows, down_proj input features);
+ *   lm_head    vocab rows.
+ * out_proj, o_proj and down_proj take the input-feature slice that matches
+ * and their fp32 partial products are summed over the ranks.  Returns
+ * IAM_EINVAL when the dims do not split over `world`. */
+typedef struct iam_tp_shard {
+  int gdn_k_head0, gdn_k_heads;
+  int gdn_v_head0, gdn_v_heads;
+  int q_head0, q_heads;
+  int kv_head0, kv_heads;
+  int inter0, inter;
+  int vocab0, vocab;
+} iam_tp_shard;
+int iam_tp_shard_of(const iam_dims* dims, int rank, int world, iam_tp_shard* out);
+
 typedef struct iam_engine iam_engine;
 
 /* Create an engine on `device` (one process per GPU).  For tensor

@@ -259,28 +259,23 @@ int build_registry(EngineImpl& e) {
   const int hd = d.head_dim, gd = d.gdn_dk;
   const int key_dim = d.gdn_k_heads * gd, vdim = d.gdn_v_heads * d.gdn_dv;
   const int conv_dim = 2 * key_dim + vdim;
-  // GDN head shards
-  e.gk_l = d.gdn_k_heads / W;
-  e.gv_l = d.gdn_v_heads / W;
-  e.k0 = r * e.gk_l;
-  e.v0 = r * e.gv_l;
+  iam_tp_shard sp;
+  E_RUN(iam_tp_shard_of(&d, r, W, &sp));
+  e.gk_l = sp.gdn_k_heads;
+  e.gv_l = sp.gdn_v_heads;
+  e.k0 = sp.gdn_k_head0;
+  e.v0 = sp.gdn_v_head0;
   e.key_l = e.gk_l * gd;
   e.vd_l = e.gv_l * d.gdn_dv;
   e.conv_l = 2 * e.key_l + e.vd_l;
-  // attention heads: KV heads split up to n_kv_heads ways, replicated beyond
-  e.hq_l = d.n_heads / W;
-  e.h0 = r * e.hq_l;
-  if (W <= d.n_kv_heads) {
-    e.hkv_l = d.n_kv_heads / W;
-    e.kv0 = r * e.hkv_l;
-  } else {
-    e.hkv_l = 1;
-    e.kv0 = r / (W / d.n_kv_heads);
-  }
-  e.inter_l = I / W;
-  e.i0 = r * e.inter_l;
-  e.vocab_l = d.vocab / W;
-  e.voff = r * e.vocab_l;
+  e.hq_l = sp.q_heads;
+  e.h0 = sp.q_head0;
+  e.hkv_l = sp.kv_heads;
+  e.kv0 = sp.kv_head0;
+  e.inter_l = sp.inter;
+  e.i0 = sp.inter0;
+  e.vocab_l = sp.vocab;
+  e.voff = sp.vocab0;
 
   Shard qkv_rows;  // q heads, k heads, v heads of this shard
   qkv_rows.rows.push_back({e.k0 * gd, (e.k0 + e.gk_l) * gd});
@@ -879,6 +874,34 @@ static int validate_dims(const iam_dims& d, int world) {
   IAM_CHECK(d.vocab % (16 * world) == 0, "dims: vocab / world must be a multiple of 16");
   IAM_CHECK(d.max_rows >= 1 && d.max_rows <= iam::kMaxRowsFinalize, "dims: max_rows in 1..256");
   IAM_CHECK(d.max_ctx >= d.max_rows, "dims: max_ctx");
+  return IAM_OK;
+}
+
+extern "C" int iam_tp_shard_of(const iam_dims* dims, int rank, int world, iam_tp_shard* out) {
+  IAM_CHECK(dims && out, "iam_tp_shard_of: null argument");
+  const int r = validate_dims(*dims, world);
+  if (r != IAM_OK) return r;
+  IAM_CHECK(rank >= 0 && rank < world, "iam_tp_shard_of: rank out of range");
+  const iam_dims& d = *dims;
+  iam_tp_shard s;
+  s.gdn_k_heads = d.gdn_k_heads / world;
+  s.gdn_k_head0 = rank * s.gdn_k_heads;
+  s.gdn_v_heads = d.gdn_v_heads / world;
+  s.gdn_v_head0 = rank * s.gdn_v_heads;
+  s.q_heads = d.n_heads / world;
+  s.q_head0 = rank * s.q_heads;
+  if (world <= d.n_kv_heads) {
+    s.kv_heads = d.n_kv_heads / world;
+    s.kv_head0 = rank * s.kv_heads;
+  } else {
+    s.kv_heads = 1;
+    s.kv_head0 = rank / (world / d.n_kv_heads);
+  }
+  s.inter = d.intermediate / world;
+  s.inter0 = rank * s.inter;
+  s.vocab = d.vocab / world;
+  s.vocab0 = rank * s.vocab;
+  *out = s;
   return IAM_OK;
 }
 

@@ -48,6 +48,7 @@ _SIGS = {
                                 _vp]),
     "iam_sdpa_decode_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "iam_dims_qwen35_27b": (None, [_vp]),
+    "iam_tp_shard_of": (_i, [_vp, _i, _i, _vp]),
     "iam_create": (_i, [_vp, _i, _i, _i, _vp, _vp]),
     "iam_nccl_unique_id": (_i, [_vp]),
     "iam_destroy": (None, [_vp]),
@@ -205,6 +206,24 @@ class Dims(C.Structure):
         for k, v in over.items():
             setattr(d, k, v)
         return d
+
+
+class TpShard(C.Structure):
+    """iam_tp_shard: [first, first + count) ranges of one tensor-parallel rank."""
+    _fields_ = [(n, C.c_int) for n in (
+        "gdn_k_head0", "gdn_k_heads", "gdn_v_head0", "gdn_v_heads", "q_head0", "q_heads", "kv_head0", "kv_heads",
+        "inter0", "inter", "vocab0", "vocab")]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+def tp_shard_of(dims: Dims, rank: int, world: int) -> TpShard:
+    """The shard the engine of `rank` holds when the model is split over `world`
+    GPUs (host only; needs no GPU)."""
+    out = TpShard()
+    _check(lib().iam_tp_shard_of(C.byref(dims), rank, world, C.byref(out)))
+    return out
 
 
 def nccl_unique_id() -> bytes:

@@ -148,12 +148,13 @@ def _dequant_rows(w, s, b, r0, r1, group):
     return hit[1]
 
 
-def qmm_affine4(x, w, s, b, group: int = 64, row_chunk: int = 8192) -> np.ndarray:
+def qmm_affine4(x, w, s, b, group: int = 64, row_chunk: int = 8192, round_out: bool = True) -> np.ndarray:
     """y[M, N] = bf16(x[M, K] . dequant(W)[N, K]^T), fp32 accumulation.
 
     The MLX qmm as dispatched by dispatchQMatmul (full_forward.swift:711-728) and
     encodeQMM (batch_verify_27b.swift:100-119); semantics = mx.dequantize ->
-    matmul (kernel_dispatch.swift:6-14)."""
+    matmul (kernel_dispatch.swift:6-14).  ``round_out=False`` keeps the fp32
+    accumulator (a tensor-parallel partial product before its all-reduce)."""
     x = np.asarray(x, np.float32)
     squeeze = x.ndim == 1
     x2 = x.reshape(1, -1) if squeeze else x
@@ -163,7 +164,8 @@ def qmm_affine4(x, w, s, b, group: int = 64, row_chunk: int = 8192) -> np.ndarra
         r1 = min(n, r0 + row_chunk)
         wd = _dequant_rows(w, s, b, r0, r1, group)
         y[:, r0:r1] = x2 @ wd.T
-    y = bf16(y)
+    if round_out:
+        y = bf16(y)
     return y[0] if squeeze else y
 
 
@@ -345,17 +347,19 @@ def sdpa_decode(q, k_cache, v_cache, seq_len: int) -> np.ndarray:
 # layers and the model step
 # --------------------------------------------------------------------------
 
-def mlp(normed, W, prefix):
-    """dispatchMLP (full_forward.swift:1167-1190)."""
+def mlp(normed, W, prefix, rowpar=qmm_affine4):
+    """dispatchMLP (full_forward.swift:1167-1190).  ``rowpar`` is the down_proj
+    matmul (the tensor-parallel variant sums partial products over ranks)."""
     gate = qmm_affine4(normed, *W[prefix + "mlp.gate_proj"])
     up = qmm_affine4(normed, *W[prefix + "mlp.up_proj"])
-    return qmm_affine4(silu_multiply(gate, up), *W[prefix + "mlp.down_proj"])
+    return rowpar(silu_multiply(gate, up), *W[prefix + "mlp.down_proj"])
 
 
-def gdn_block(hidden, W, prefix, conv_state, S, dims: Dims):
+def gdn_block(hidden, W, prefix, conv_state, S, dims: Dims, rowpar=qmm_affine4):
     """dispatchGDNLayer (full_forward.swift:993-1161) for M tokens run as M sequential
     decode steps.  hidden [M, H] bf16; conv_state [3, C] bf16 and S [Hv, dv, dk] fp32
-    are updated in place.  Returns the new hidden [M, H]."""
+    are updated in place.  Returns the new hidden [M, H].  ``rowpar`` is the
+    out_proj / down_proj matmul."""
     d = dims
     normed = rms_norm(hidden, W[prefix + "input_layernorm.weight"], d.eps)
     qkv = qmm_affine4(normed, *W[prefix + "linear_attn.in_proj_qkv"])
@@ -379,16 +383,17 @@ def gdn_block(hidden, W, prefix, conv_state, S, dims: Dims):
         g, beta = compute_g_beta(aproj[t], bproj[t], A_log, dt_bias)
         y = gated_delta_step(qn, kn, v, g, beta, S)
         gn[t] = rms_norm_gated(y, z[t].reshape(d.gdn_v_heads, d.gdn_dv), normw, d.eps).reshape(-1)
-    out = qmm_affine4(gn, *W[prefix + "linear_attn.out_proj"])
+    out = rowpar(gn, *W[prefix + "linear_attn.out_proj"])
     resid = residual_add(hidden, out)
     normed2 = rms_norm(resid, W[prefix + "post_attention_layernorm.weight"], d.eps)
-    return residual_add(resid, mlp(normed2, W, prefix))
+    return residual_add(resid, mlp(normed2, W, prefix, rowpar))
 
 
-def attn_block(hidden, W, prefix, k_cache, v_cache, pos: int, dims: Dims):
+def attn_block(hidden, W, prefix, k_cache, v_cache, pos: int, dims: Dims, rowpar=qmm_affine4):
     """dispatchAttnLayer (full_forward.swift:828-987) for M tokens at positions
     pos..pos+M-1 (causal inside the block).  Caches [T, Hkv, d] bf16 are appended
-    in place: k is normed+roped, v raw (full_forward.swift:909-924)."""
+    in place: k is normed+roped, v raw (full_forward.swift:909-924).  ``rowpar``
+    is the o_proj / down_proj matmul."""
     d = dims
     m = hidden.shape[0]
     normed = rms_norm(hidden, W[prefix + "input_layernorm.weight"], d.eps)
@@ -413,10 +418,10 @@ def attn_block(hidden, W, prefix, k_cache, v_cache, pos: int, dims: Dims):
         qn, gate = qs[t]
         att = sdpa_decode(qn, k_cache, v_cache, pos + t + 1)
         gated[t] = sigmoid_multiply(att.reshape(-1), gate.reshape(-1))
-    o = qmm_affine4(gated, *W[prefix + "self_attn.o_proj"])
+    o = rowpar(gated, *W[prefix + "self_attn.o_proj"])
     resid = residual_add(hidden, o)
     normed2 = rms_norm(resid, W[prefix + "post_attention_layernorm.weight"], d.eps)
-    return residual_add(resid, mlp(normed2, W, prefix))
+    return residual_add(resid, mlp(normed2, W, prefix, rowpar))
 
 
 def accept_length(tokens, argmax) -> int:
@@ -436,21 +441,24 @@ class State:
     v_cache: dict
 
 
-def model_step(tokens, pos: int, W, state: State, dims: Dims, return_hidden: bool = False):
+def model_step(tokens, pos: int, W, state: State, dims: Dims, return_hidden: bool = False,
+               rowpar=qmm_affine4, lm_argmax=argmax_first):
     """forwardPass (full_forward.swift:1198-1308) for a verify block of K tokens at
     positions pos..pos+K-1: embedding, 64-layer loop, final norm, lm_head, argmax.
-    Returns (argmax [K], accept_len[, final normed hidden])."""
+    Returns (argmax [K], accept_len[, final normed hidden, logits]).  ``rowpar``
+    and ``lm_argmax`` are the hooks the tensor-parallel restatement
+    (oracle/tp.py) replaces."""
     d = dims
     hidden = embed_lookup_bf16_table(W["model.embed_tokens.weight"], tokens)
     for li in range(d.n_layers):
         prefix = f"model.layers.{li}."
         if d.is_full_attn(li):
-            hidden = attn_block(hidden, W, prefix, state.k_cache[li], state.v_cache[li], pos, d)
+            hidden = attn_block(hidden, W, prefix, state.k_cache[li], state.v_cache[li], pos, d, rowpar)
         else:
-            hidden = gdn_block(hidden, W, prefix, state.conv[li], state.S[li], d)
+            hidden = gdn_block(hidden, W, prefix, state.conv[li], state.S[li], d, rowpar)
     normed = rms_norm(hidden, W["model.norm.weight"], d.eps)
     logits = qmm_affine4(normed, *W["lm_head"])
-    am = argmax_first(logits)
+    am = lm_argmax(logits)
     out = (am, accept_length(tokens, am))
     if return_hidden:
         out = out + (normed, logits)
