@@ -146,9 +146,10 @@ struct TcLayout {
   static constexpr int kWOff = kXS * kXBytes;              // weight ring after the (1 KiB aligned) x ring
   static constexpr int kBarOff = kWOff + kWS * kQpBlockBytes;
   // wfull, wempty [kWS]; xfull, xempty [kXS]; afull, aempty [kTcASlots];
-  // dfull; then the TMEM base and flags
+  // dfull; then the TMEM base and flags (64 bytes) and this CTA's segment
   static constexpr int kNumBars = 2 * kWS + 2 * kXS + 2 * kTcASlots + 1;
-  static constexpr int kSmem = kBarOff + kNumBars * 8 + 64 + 1024;  // + alignment slack
+  static constexpr int kSmem = kBarOff + kNumBars * 8 + 64 + 128 + 1024;  // + alignment slack
+  static_assert(sizeof(QmmSeg) <= 128, "segment copy");
   static_assert(kXBytes % 1024 == 0, "x stages must keep 1 KiB alignment");
   // more than half an SM's shared memory: one CTA (512 TMEM columns) per SM
   static_assert(kSmem > 116 * 1024 && kSmem <= 227 * 1024, "one CTA per SM");
@@ -182,8 +183,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
 #pragma unroll
   for (int i = 1; i < kQmmMaxSeg; ++i)
     if (i < A.nseg && bx >= A.seg[i].cta_begin) si = i;
-  const QmmSeg& S = A.seg[si];
-  const int tile = bx - S.cta_begin;
+  // The CTA's segment is read from a shared-memory copy: a parameter struct
+  // indexed at run time is read through the generic path, hundreds of cycles
+  // a field while the weight stream fills the memory system.
+  QmmSeg* seg_copy = reinterpret_cast<QmmSeg*>(tail + 64);
+  int tile = bx;
+#pragma unroll
+  for (int i = 0; i < kQmmMaxSeg; ++i)
+    if (i == si) tile = bx - A.seg[i].cta_begin;
   const int KB = (A.K + kQpBlockK - 1) / kQpBlockK;
   const int KS = gridDim.z, ks = blockIdx.z;
   const int kb0 = (ks * KB) / KS, kb1 = ((ks + 1) * KB) / KS, nkb = kb1 - kb0;
@@ -203,6 +210,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     }
     mbar_init(dfull, 1);
     *abort_flag = 0;
+#pragma unroll
+    for (int i = 0; i < kQmmMaxSeg; ++i)  // constant indices: constant-bank loads
+      if (i == si) *seg_copy = A.seg[i];
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -214,6 +224,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const QmmSeg& S = *seg_copy;
   pdl_trigger();
 
   auto give_up = [&]() {
@@ -436,13 +447,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         }
         named_bar_sync(1, 32 * kTcDqWarps);
         const int f = tile * 64 + row;
+        uint16_t* const out = S.out;
+        const size_t ldo = static_cast<size_t>(S.ldo);
+        const int M = A.M;
         if (row < 64 && f < S.rows) {
 #pragma unroll
           for (int e = 0; e < EC; ++e) {
             const int tok = tok0 + e;
-            if (tok < A.M)
-              S.out[static_cast<size_t>(tok) * S.ldo + f] =
-                  f2bf(silu_f(round_bf(v[e])) * round_bf(ubuf[row * NN + tok]));
+            if (tok < M) out[tok * ldo + f] = f2bf(silu_f(round_bf(v[e])) * round_bf(ubuf[row * NN + tok]));
           }
         }
       } else if (mode == EPI_ARGMAX) {
@@ -469,18 +481,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         }
       } else {
         const int grow = tile * kQpRows + row;
+        // the fields in registers: the stores would make the compiler re-read
+        // them every token otherwise
+        uint16_t* const out = S.out;
+        float* const out32 = S.out32;
+        const uint16_t* const resid = S.resid;
+        const size_t ldo = static_cast<size_t>(S.ldo), ldr = static_cast<size_t>(S.ldr);
+        const int M = A.M;
         if (grow < S.rows) {
 #pragma unroll
           for (int e = 0; e < EC; ++e) {
             const int tok = tok0 + e;
-            if (tok >= A.M) continue;
-            const size_t o = static_cast<size_t>(tok) * S.ldo + grow;
+            if (tok >= M) continue;
+            const size_t o = tok * ldo + grow;
             if (mode == EPI_F32) {
-              S.out32[o] = v[e];
+              out32[o] = v[e];
             } else if (mode == EPI_RESID) {
-              S.out[o] = f2bf(bf2f(S.resid[static_cast<size_t>(tok) * S.ldr + grow]) + round_bf(v[e]));
+              out[o] = f2bf(bf2f(resid[tok * ldr + grow]) + round_bf(v[e]));
             } else {
-              S.out[o] = f2bf(v[e]);
+              out[o] = f2bf(v[e]);
             }
           }
         }
