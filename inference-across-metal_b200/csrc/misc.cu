@@ -20,11 +20,19 @@ __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restric
                                                        const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
                                                        int ldo, int dim, float eps) {
   extern __shared__ __align__(16) uint4 xs[];  // the row, staged in one round of loads
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int nv = dim / 8;
+  // the norm weights do not depend on the preceding kernel: fetch them first
+  // (dim <= 16384 and 512 threads: at most four 8-element chunks a thread)
+  uint4 wreg[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = tid + r * static_cast<int>(blockDim.x);
+    if (i < nv) wreg[r] = *reinterpret_cast<const uint4*>(w + 8 * i);
+  }
   pdl_wait();
   pdl_trigger();
-  const int row = blockIdx.x, tid = threadIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ldx);
-  const int nv = dim / 8;
   for (int i = tid; i < nv; i += blockDim.x) xs[i] = xr[i];
   __syncthreads();
   __shared__ float rms_s;
@@ -60,9 +68,12 @@ __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restric
   __syncthreads();
   const float rms = rms_s;
   uint16_t* orow = out + static_cast<size_t>(row) * ldo;
-  for (int i = tid; i < nv; i += blockDim.x) {
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = tid + r * static_cast<int>(blockDim.x);
+    if (i >= nv) break;
     const uint4 v = xs[i];
-    const uint4 ww = *reinterpret_cast<const uint4*>(w + 8 * i);
+    const uint4 ww = wreg[r];
     const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, wv[4] = {ww.x, ww.y, ww.z, ww.w};
     uint32_t o[4];
 #pragma unroll
