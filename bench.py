@@ -287,23 +287,36 @@ def profile_step(args):
 
 
 def profile_qmm(args):
-    """A few launches of one W4A16 matmul shape N,K,M (random codes, packed as
-    the engine packs them) through the tensor-core kernel, for ncu."""
+    """A few launches of W4A16 matmul shapes "N,K,M[,mlx];..." (random codes)
+    for ncu: through the tensor-core kernel on packed weights, or, with a
+    fourth field "mlx", through the mma.sync kernel on the MLX layout (the
+    crossover pair)."""
+    for spec in args.profile_qmm.split(";"):
+        _profile_one_qmm(spec)
+
+
+def _profile_one_qmm(spec):
     import torch
     import iam_b200 as I
-    N, K, M = (int(v) for v in args.profile_qmm.split(","))
+    f = spec.split(",")
+    N, K, M = (int(v) for v in f[:3])
+    mlx = len(f) > 3 and f[3] == "mlx"
     g = torch.Generator(device="cuda").manual_seed(0)
     w = torch.randint(-2**31, 2**31 - 1, (N, K // 8), dtype=torch.int32, device="cuda", generator=g)
     s = (torch.rand(N, K // 64, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     b = (-8 * s.float()).to(torch.bfloat16)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    pk = torch.empty(I.qmm_packed_bytes(N, K), dtype=torch.uint8, device="cuda")
-    I.qmm_pack_affine4(w.data_ptr(), s.data_ptr(), b.data_ptr(), pk.data_ptr(), N, K)
-    for _ in range(4):
-        I.qmm_affine4_packed(pk.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K)
+    if mlx:
+        for _ in range(4):
+            I.qmm_affine4(w.data_ptr(), s.data_ptr(), b.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K)
+    else:
+        pk = torch.empty(I.qmm_packed_bytes(N, K), dtype=torch.uint8, device="cuda")
+        I.qmm_pack_affine4(w.data_ptr(), s.data_ptr(), b.data_ptr(), pk.data_ptr(), N, K)
+        for _ in range(4):
+            I.qmm_affine4_packed(pk.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K)
     torch.cuda.synchronize()
-    print(json.dumps({"profile_qmm": [N, K, M]}))
+    print(json.dumps({"profile_qmm": [N, K, M], "kernel": "mma.sync" if mlx else "tcgen05"}))
 
 
 def main():
@@ -315,7 +328,8 @@ def main():
     ap.add_argument("--impl", default="iam")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--profile-step", action="store_true", help="two graph steps at --k, for ncu launch lists")
-    ap.add_argument("--profile-qmm", default=None, help="N,K,M: a few launches of one matmul, for ncu")
+    ap.add_argument("--profile-qmm", default=None,
+                    help="N,K,M[,mlx];...: a few launches of each matmul (tensor-core, or mma.sync on the MLX layout), for ncu")
     args = ap.parse_args()
     if args.profile_step:
         return profile_step(args)
