@@ -33,70 +33,78 @@ struct GdnSmem {
   float beta[kChunk];
 };
 
-// Sum p[0..7] over the warp; lane l gets the sum of row rr(l) =
-// 4*bit4(l) + 2*bit3(l) + bit2(l).
-__device__ __forceinline__ float reduce8(float (&p)[8], int lane) {
-  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+// Sum a[0..7] and b[0..7] over the warp in five dependent exchange steps:
+// lane l ends with the sum of a[row] (bit 4 of l clear) or b[row] (set), row =
+// 4*bit3(l) + 2*bit2(l) + bit1(l); lanes l and l^1 hold the same sum.
+__device__ __forceinline__ float reduce16(const float (&a)[8], const float (&b)[8], int lane) {
+  float v[8];
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float send = b4 ? a[i] : b[i];
+    const float keep = b4 ? b[i] : a[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float send = b4 ? p[i] : p[i + 4];
-    const float keep = b4 ? p[i + 4] : p[i];
-    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    const float send = b3 ? v[i] : v[i + 4];
+    const float keep = b3 ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
   }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const float send = b3 ? p[i] : p[i + 2];
-    const float keep = b3 ? p[i + 2] : p[i];
-    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    const float send = b2 ? v[i] : v[i + 2];
+    const float keep = b2 ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
   }
   {
-    const float send = b2 ? p[0] : p[1];
-    const float keep = b2 ? p[1] : p[0];
-    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    const float send = b1 ? v[0] : v[1];
+    const float keep = b1 ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
   }
-  float r = p[0];
-  r += __shfl_xor_sync(0xffffffffu, r, 2);
-  r += __shfl_xor_sync(0xffffffffu, r, 1);
-  return r;
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
-__device__ __forceinline__ int row_of_lane(int lane) {
-  return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-}
-__device__ __forceinline__ int lane_of_row(int r) { return ((r >> 2) & 1) * 16 + ((r >> 1) & 1) * 8 + (r & 1) * 4; }
+// the first lane holding row r of the `a` sums of reduce16
+__device__ __forceinline__ int lane_of_row16(int r) { return ((r >> 2) & 1) * 8 + ((r >> 1) & 1) * 4 + (r & 1) * 2; }
 
 // gated_delta_step_bf16 (full_forward.swift:321-355) for tokens [0, n) of the
 // chunk in shared memory: S = g*S; kv = S.k; delta = beta*(v - kv);
 // S = S + k*delta; y = bf16(S.q).  S[r][i] = state[dv = 8w + r][dk = 4l + i].
+// Per token one warp reduction carries both y_t = S_t.q_t and the next
+// token's S_t.k_{t+1} (kv_{t+1} = g_{t+1} * S_t.k_{t+1}, the same product in
+// another order), so the serial chain holds one reduction a token, not two.
 __device__ __forceinline__ void delta_chunk(float (&S)[8][4], const GdnSmem& sm, float (*ys)[kHD], int n, int warp,
                                             int lane) {
-  const int rr = row_of_lane(lane);
+  const int rr = ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+  const bool is_y = lane & 16;
+  float a[8], b[8];
+  {
+    const float4 k4 = *reinterpret_cast<const float4*>(&sm.k[0][4 * lane]);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      a[r] = fmaf(S[r][3], k4.w, fmaf(S[r][2], k4.z, fmaf(S[r][1], k4.y, S[r][0] * k4.x)));
+      b[r] = 0.f;
+    }
+  }
+  float red = reduce16(a, b, lane);  // lanes without bit 4: S.k_0 of row rr
   for (int t = 0; t < n; ++t) {
     const float gv = sm.g[t], bv = sm.beta[t];
     const float4 k4 = *reinterpret_cast<const float4*>(&sm.k[t][4 * lane]);
     const float4 q4 = *reinterpret_cast<const float4*>(&sm.q[t][4 * lane]);
-    float p[8];
+    const float4 kn = t + 1 < n ? *reinterpret_cast<const float4*>(&sm.k[t + 1][4 * lane]) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float dmine = (sm.v[t][8 * warp + rr] - gv * red) * bv;  // meaningful in the lanes holding S.k
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-      S[r][0] = S[r][0] * gv;
-      S[r][1] = S[r][1] * gv;
-      S[r][2] = S[r][2] * gv;
-      S[r][3] = S[r][3] * gv;
-      p[r] = fmaf(S[r][3], k4.w, fmaf(S[r][2], k4.z, fmaf(S[r][1], k4.y, S[r][0] * k4.x)));
+      const float d = __shfl_sync(0xffffffffu, dmine, lane_of_row16(r));
+      S[r][0] = fmaf(S[r][0], gv, k4.x * d);
+      S[r][1] = fmaf(S[r][1], gv, k4.y * d);
+      S[r][2] = fmaf(S[r][2], gv, k4.z * d);
+      S[r][3] = fmaf(S[r][3], gv, k4.w * d);
+      b[r] = fmaf(S[r][3], q4.w, fmaf(S[r][2], q4.z, fmaf(S[r][1], q4.y, S[r][0] * q4.x)));
+      a[r] = fmaf(S[r][3], kn.w, fmaf(S[r][2], kn.z, fmaf(S[r][1], kn.y, S[r][0] * kn.x)));
     }
-    const float kv = reduce8(p, lane);
-    const float dmine = (sm.v[t][8 * warp + rr] - kv) * bv;
-    float q_part[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const float d = __shfl_sync(0xffffffffu, dmine, lane_of_row(r));
-      S[r][0] = S[r][0] + k4.x * d;
-      S[r][1] = S[r][1] + k4.y * d;
-      S[r][2] = S[r][2] + k4.z * d;
-      S[r][3] = S[r][3] + k4.w * d;
-      q_part[r] = fmaf(S[r][3], q4.w, fmaf(S[r][2], q4.z, fmaf(S[r][1], q4.y, S[r][0] * q4.x)));
-    }
-    const float y = reduce8(q_part, lane);
-    if ((lane & 3) == 0) ys[t][8 * warp + rr] = round_bf(y);
+    red = reduce16(a, b, lane);
+    if (is_y && (lane & 1) == 0) ys[t][8 * warp + rr] = round_bf(red);
   }
 }
 
