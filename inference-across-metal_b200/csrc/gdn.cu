@@ -15,6 +15,8 @@
 // Conv outputs, q^, k^, v, g, beta of a chunk of tokens are prepared in
 // parallel in shared memory before the sequential part; the gated norm runs
 // after it, again in parallel over tokens.
+#include <cstdlib>
+
 #include "kernels.cuh"
 
 namespace iam {
@@ -31,118 +33,154 @@ struct GdnSmem {
   float y[kChunk][kHD];
   float g[kChunk];
   float beta[kChunk];
+  float ssx[2][kChunk];  // partial sums of y^2 of this CTA's rows (cluster exchange), by chunk parity
 };
 
-// Sum a[0..7] and b[0..7] over the warp in five dependent exchange steps:
-// lane l ends with the sum of a[row] (bit 4 of l clear) or b[row] (set), row =
-// 4*bit3(l) + 2*bit2(l) + bit1(l); lanes l and l^1 hold the same sum.
-__device__ __forceinline__ float reduce16(const float (&a)[8], const float (&b)[8], int lane) {
-  float v[8];
-  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float send = b4 ? a[i] : b[i];
-    const float keep = b4 ? b[i] : a[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float send = b3 ? v[i] : v[i + 4];
-    const float keep = b3 ? v[i + 4] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float send = b2 ? v[i] : v[i + 2];
-    const float keep = b2 ? v[i + 2] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-  {
-    const float send = b1 ? v[0] : v[1];
-    const float keep = b1 ? v[1] : v[0];
-    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-  }
-  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
-// the first lane holding row r of the `a` sums of reduce16
-__device__ __forceinline__ int lane_of_row16(int r) { return ((r >> 2) & 1) * 8 + ((r >> 1) & 1) * 4 + (r & 1) * 2; }
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// a float in the shared memory of CTA `rank` of the cluster, at this CTA's address of p
+__device__ __forceinline__ float ld_peer(const float* p, uint32_t rank) {
+  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p)), ra;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
+// Sum v[0..V-1] (V/2 "a" partials, then V/2 "b" partials) over the warp in
+// five dependent exchange steps.  Lane l ends with the sum of a[row] (bit 4
+// of l clear) or b[row] (set); the row is made of the next log2(V/2) bits of
+// l below bit 4, most significant first, and the remaining low bits select
+// lanes holding the same sum.
+template <int V>
+__device__ __forceinline__ float xreduce(float (&v)[V], int lane) {
+  int n = V;
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    if (n > 1) {
+      const bool up = lane & m;
+      const int h = n / 2;
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) {
+        if (i < h) {
+          const float send = up ? v[i] : v[i + h];
+          const float keep = up ? v[i + h] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+      }
+      n = h;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+    }
+  }
+  return v[0];
+}
+template <int RPW>
+struct RowMap {
+  static constexpr int kLog = RPW == 8 ? 3 : RPW == 4 ? 2 : RPW == 2 ? 1 : 0;
+  static constexpr int kShift = 4 - kLog;  // lane bits below the row bits
+  __device__ static int row(int lane) { return (lane >> kShift) & (RPW - 1); }
+  __device__ static int lane_of(int r) { return r << kShift; }
+  __device__ static bool writer(int lane) { return (lane & ((1 << kShift) - 1)) == 0; }
+};
 
 // gated_delta_step_bf16 (full_forward.swift:321-355) for tokens [0, n) of the
 // chunk in shared memory: S = g*S; kv = S.k; delta = beta*(v - kv);
-// S = S + k*delta; y = bf16(S.q).  S[r][i] = state[dv = 8w + r][dk = 4l + i].
-// Per token one warp reduction carries both y_t = S_t.q_t and the next
-// token's S_t.k_{t+1} (kv_{t+1} = g_{t+1} * S_t.k_{t+1}, the same product in
-// another order), so the serial chain holds one reduction a token, not two.
-__device__ __forceinline__ void delta_chunk(float (&S)[8][4], const GdnSmem& sm, float (*ys)[kHD], int n, int warp,
-                                            int lane) {
-  const int rr = ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+// S = S + k*delta; y = bf16(S.q).  The warp holds RPW rows of S:
+// S[r][i] = state[dv = row0 + RPW*w + r][dk = 4l + i].  Per token one warp
+// reduction carries both y_t = S_t.q_t and the next token's S_t.k_{t+1}
+// (kv_{t+1} = g_{t+1} * S_t.k_{t+1}, the same product in another order), so
+// the serial chain holds one reduction a token, not two.
+template <int RPW>
+__device__ __forceinline__ void delta_chunk(float (&S)[RPW][4], const GdnSmem& sm, float (*ys)[kHD], int n,
+                                            int row0, int lane) {
+  using RM = RowMap<RPW>;
+  const int rr = RM::row(lane);
   const bool is_y = lane & 16;
-  float a[8], b[8];
+  float v[2 * RPW];
   {
     const float4 k4 = *reinterpret_cast<const float4*>(&sm.k[0][4 * lane]);
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      a[r] = fmaf(S[r][3], k4.w, fmaf(S[r][2], k4.z, fmaf(S[r][1], k4.y, S[r][0] * k4.x)));
-      b[r] = 0.f;
+    for (int r = 0; r < RPW; ++r) {
+      v[r] = fmaf(S[r][3], k4.w, fmaf(S[r][2], k4.z, fmaf(S[r][1], k4.y, S[r][0] * k4.x)));
+      v[RPW + r] = 0.f;
     }
   }
-  float red = reduce16(a, b, lane);  // lanes without bit 4: S.k_0 of row rr
+  float red = xreduce<2 * RPW>(v, lane);  // lanes without bit 4: S.k_0 of row rr
   for (int t = 0; t < n; ++t) {
     const float gv = sm.g[t], bv = sm.beta[t];
     const float4 k4 = *reinterpret_cast<const float4*>(&sm.k[t][4 * lane]);
     const float4 q4 = *reinterpret_cast<const float4*>(&sm.q[t][4 * lane]);
     const float4 kn = t + 1 < n ? *reinterpret_cast<const float4*>(&sm.k[t + 1][4 * lane]) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float dmine = (sm.v[t][8 * warp + rr] - gv * red) * bv;  // meaningful in the lanes holding S.k
+    const float dmine = (sm.v[t][row0 + rr] - gv * red) * bv;  // meaningful in the lanes holding S.k
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const float d = __shfl_sync(0xffffffffu, dmine, lane_of_row16(r));
+    for (int r = 0; r < RPW; ++r) {
+      const float d = __shfl_sync(0xffffffffu, dmine, RM::lane_of(r));
       S[r][0] = fmaf(S[r][0], gv, k4.x * d);
       S[r][1] = fmaf(S[r][1], gv, k4.y * d);
       S[r][2] = fmaf(S[r][2], gv, k4.z * d);
       S[r][3] = fmaf(S[r][3], gv, k4.w * d);
-      b[r] = fmaf(S[r][3], q4.w, fmaf(S[r][2], q4.z, fmaf(S[r][1], q4.y, S[r][0] * q4.x)));
-      a[r] = fmaf(S[r][3], kn.w, fmaf(S[r][2], kn.z, fmaf(S[r][1], kn.y, S[r][0] * kn.x)));
+      v[RPW + r] = fmaf(S[r][3], q4.w, fmaf(S[r][2], q4.z, fmaf(S[r][1], q4.y, S[r][0] * q4.x)));
+      v[r] = fmaf(S[r][3], kn.w, fmaf(S[r][2], kn.z, fmaf(S[r][1], kn.y, S[r][0] * kn.x)));
     }
-    red = reduce16(a, b, lane);
-    if (is_y && (lane & 1) == 0) ys[t][8 * warp + rr] = round_bf(red);
+    red = xreduce<2 * RPW>(v, lane);
+    if (is_y && RM::writer(lane)) ys[t][row0 + rr] = round_bf(red);
   }
 }
 
-__device__ __forceinline__ void load_state(float (&S)[8][4], const float* Sh, int warp, int lane) {
+template <int RPW>
+__device__ __forceinline__ void load_state(float (&S)[RPW][4], const float* Sh, int row0, int lane) {
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const float4 v = *reinterpret_cast<const float4*>(Sh + (8 * warp + r) * kHD + 4 * lane);
+  for (int r = 0; r < RPW; ++r) {
+    const float4 v = *reinterpret_cast<const float4*>(Sh + (row0 + r) * kHD + 4 * lane);
     S[r][0] = v.x;
     S[r][1] = v.y;
     S[r][2] = v.z;
     S[r][3] = v.w;
   }
 }
-__device__ __forceinline__ void store_state(const float (&S)[8][4], float* Sh, int warp, int lane) {
+template <int RPW>
+__device__ __forceinline__ void store_state(const float (&S)[RPW][4], float* Sh, int row0, int lane) {
 #pragma unroll
-  for (int r = 0; r < 8; ++r)
-    *reinterpret_cast<float4*>(Sh + (8 * warp + r) * kHD + 4 * lane) = make_float4(S[r][0], S[r][1], S[r][2], S[r][3]);
+  for (int r = 0; r < RPW; ++r)
+    *reinterpret_cast<float4*>(Sh + (row0 + r) * kHD + 4 * lane) = make_float4(S[r][0], S[r][1], S[r][2], S[r][3]);
 }
 
+// One V-head over a cluster of C CTAs: CTA j of the cluster holds state rows
+// dv = 128j/C .. 128(j+1)/C - 1 (rows evolve independently), prepares the
+// head's q^, k^ and its own v rows, runs the recurrence on its rows, and the
+// gated norm's sum of squares over dv is exchanged through distributed
+// shared memory (summed in rank order).  C = 1 is the one-CTA-a-head kernel.
+template <int C>
 __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a) {
+  constexpr int R = kHD / C, RPW = R / (kThreads / 32);
   extern __shared__ __align__(16) unsigned char smem_raw[];
   GdnSmem& sm = *reinterpret_cast<GdnSmem*>(smem_raw);
-  const int h = blockIdx.x;
+  const int h = blockIdx.x / C;
+  const int jr = C == 1 ? 0 : static_cast<int>(cluster_rank());
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rep = a.n_v_heads / a.n_k_heads;
   const int kh = h / rep;
   float* Sh = a.S + static_cast<size_t>(h) * kHD * kHD;
+  const int row0 = jr * R + warp * RPW;  // this warp's first state row
 
   // The state does not depend on the preceding kernel: load it before waiting.
-  float S[8][4];
-  load_state(S, Sh, warp, lane);
+  float S[RPW][4];
+  load_state<RPW>(S, Sh, row0, lane);
   pdl_wait();
   pdl_trigger();
   const bool swap = a.parity_dev && *a.parity_dev;
   const uint16_t* conv_in = swap ? a.conv_out : a.conv_in;
   uint16_t* conv_out = swap ? const_cast<uint16_t*>(a.conv_in) : a.conv_out;
 
-  // conv channel of this thread: 0..127 q (K-head kh), 128..255 k, 256..383 v (V-head h)
+  // conv channel of this thread: 0..127 q (K-head kh), 128..255 k, then this
+  // CTA's R v rows (V-head h)
   const int ct = threadIdx.x;
   int col = -1, region = -1, c = ct & 127;
   if (ct < 128) {
@@ -151,7 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   } else if (ct < 256) {
     col = a.key_dim + kh * kHD + c;
     region = 1;
-  } else if (ct < 384) {
+  } else if (ct < 256 + R) {
+    c = jr * R + (ct - 256);
     col = 2 * a.key_dim + h * kHD + c;
     region = 2;
   }
@@ -168,7 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
     w2 = conv_in[2 * a.conv_dim + col];
   }
 
-  for (int t0 = 0; t0 < a.rows; t0 += kChunk) {
+  int chunk = 0;
+  for (int t0 = 0; t0 < a.rows; t0 += kChunk, ++chunk) {
     const int n = min(kChunk, a.rows - t0);
     // ---- A: conv + SiLU for the chunk (depthwise_conv1d_m1_bf16, silu_bf16);
     // all of the chunk's inputs are loaded before the sequential window
@@ -193,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
           w2 = xi;
         }
       }
-    } else if (ct - 384 < n) {
+    } else if (ct >= 384 && ct - 384 < n) {
       // ---- g, beta per token (compute_g_beta_bf16)
       const int t = ct - 384;
       const size_t row = static_cast<size_t>(t0 + t) * a.ld_in;
@@ -221,34 +261,54 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
       }
     }
     __syncthreads();
-    // ---- C: the recurrence
-    delta_chunk(S, sm, sm.y, n, warp, lane);
+    // ---- C: the recurrence on this CTA's rows
+    delta_chunk<RPW>(S, sm, sm.y, n, row0, lane);
     __syncthreads();
-    // ---- D: gated RMSNorm (rms_norm_gated_bf16) and store
+    // ---- D: gated RMSNorm (rms_norm_gated_bf16) and store; lanes < R / 4
+    // hold four of this CTA's rows each
+    constexpr int kLanes = R / 4;
+    float* ssx = sm.ssx[chunk & 1];
     for (int t = warp; t < n; t += kThreads / 32) {
-      const float4 y = *reinterpret_cast<const float4*>(&sm.y[t][4 * lane]);
-      const float ss = warp_sum(y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w);
-      const float rms = sqrtf(ss / 128.f + a.eps);
-      const size_t row = static_cast<size_t>(t0 + t);
-      const uint2 zz = *reinterpret_cast<const uint2*>(a.in + row * a.ld_in + a.z_col + h * kHD + 4 * lane);
-      const uint2 ww = *reinterpret_cast<const uint2*>(a.norm_w + 4 * lane);
-      const float o0 = silu_f(lo_bf(zz.x)) * ((y.x / rms) * lo_bf(ww.x));
-      const float o1 = silu_f(hi_bf(zz.x)) * ((y.y / rms) * hi_bf(ww.x));
-      const float o2 = silu_f(lo_bf(zz.y)) * ((y.z / rms) * lo_bf(ww.y));
-      const float o3 = silu_f(hi_bf(zz.y)) * ((y.w / rms) * hi_bf(ww.y));
-      *reinterpret_cast<uint2*>(a.out + row * a.ld_out + h * kHD + 4 * lane) =
-          make_uint2(pack_bf2(o0, o1), pack_bf2(o2, o3));
+      float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (lane < kLanes) y = *reinterpret_cast<const float4*>(&sm.y[t][jr * R + 4 * lane]);
+      const float part = warp_sum(y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w);
+      if (lane == 0) ssx[t] = part;
+    }
+    if constexpr (C > 1) cluster_sync_all();  // every CTA's partial sums are in place
+    else __syncthreads();
+    for (int t = warp; t < n; t += kThreads / 32) {
+      float ss = ssx[t];
+      if constexpr (C > 1) {
+        ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < C; ++j) ss += ld_peer(&ssx[t], static_cast<uint32_t>(j));
+      }
+      if (lane < kLanes) {
+        const float4 y = *reinterpret_cast<const float4*>(&sm.y[t][jr * R + 4 * lane]);
+        const float rms = sqrtf(ss / 128.f + a.eps);
+        const size_t row = static_cast<size_t>(t0 + t);
+        const int d0 = jr * R + 4 * lane;
+        const uint2 zz = *reinterpret_cast<const uint2*>(a.in + row * a.ld_in + a.z_col + h * kHD + d0);
+        const uint2 ww = *reinterpret_cast<const uint2*>(a.norm_w + d0);
+        const float o0 = silu_f(lo_bf(zz.x)) * ((y.x / rms) * lo_bf(ww.x));
+        const float o1 = silu_f(hi_bf(zz.x)) * ((y.y / rms) * hi_bf(ww.x));
+        const float o2 = silu_f(lo_bf(zz.y)) * ((y.z / rms) * lo_bf(ww.y));
+        const float o3 = silu_f(hi_bf(zz.y)) * ((y.w / rms) * hi_bf(ww.y));
+        *reinterpret_cast<uint2*>(a.out + row * a.ld_out + h * kHD + d0) =
+            make_uint2(pack_bf2(o0, o1), pack_bf2(o2, o3));
+      }
     }
     __syncthreads();
   }
-  store_state(S, Sh, warp, lane);
+  store_state<RPW>(S, Sh, row0, lane);
   // new conv state = the last three inputs; q/k channels are shared by the
-  // `rep` V-heads of a K-head, the first of them writes them
-  if (col >= 0 && (region == 2 || h % rep == 0)) {
+  // `rep` V-heads of a K-head, the first CTA of the first of them writes them
+  if (col >= 0 && (region == 2 || (h % rep == 0 && jr == 0))) {
     conv_out[col] = w0;
     conv_out[a.conv_dim + col] = w1;
     conv_out[2 * a.conv_dim + col] = w2;
   }
+  if constexpr (C > 1) cluster_sync_all();  // no CTA leaves while a peer may read its shared memory
 }
 
 // The operator-level gated_delta_step: q^, k^ (K-head layout), v, g, beta given.
@@ -262,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1) gated_delta_kernel(const uint16_t
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* Sh = Sg + static_cast<size_t>(h) * kHD * kHD;
   float S[8][4];
-  load_state(S, Sh, warp, lane);
+  load_state<8>(S, Sh, 8 * warp, lane);
   for (int t0 = 0; t0 < rows; t0 += kChunk) {
     const int n = min(kChunk, rows - t0);
     for (int i = threadIdx.x; i < n * kHD; i += kThreads) {
@@ -277,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) gated_delta_kernel(const uint16_t
       sm.beta[threadIdx.x] = bf2f(beta[static_cast<size_t>(t0 + threadIdx.x) * n_v + h]);
     }
     __syncthreads();
-    delta_chunk(S, sm, sm.y, n, warp, lane);
+    delta_chunk<8>(S, sm, sm.y, n, 8 * warp, lane);
     __syncthreads();
     for (int i = threadIdx.x; i < n * kHD; i += kThreads) {
       const int t = i / kHD, e = i % kHD;
@@ -285,10 +345,11 @@ __global__ void __launch_bounds__(kThreads, 1) gated_delta_kernel(const uint16_t
     }
     __syncthreads();
   }
-  store_state(S, Sh, warp, lane);
+  store_state<8>(S, Sh, 8 * warp, lane);
 }
 
 bool g_attr_done = false;
+int g_sms = 148;
 }  // namespace
 
 int gdn_init_attrs();
@@ -298,10 +359,58 @@ int ensure_attrs() { return gdn_init_attrs(); }
 
 int gdn_init_attrs() {
   if (g_attr_done) return IAM_OK;
-  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
+  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
+  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
+  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
+  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
+  int dev = 0;
+  IAM_CUDA(cudaGetDevice(&dev));
+  IAM_CUDA(cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev));
   IAM_CUDA(cudaFuncSetAttribute(gated_delta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
   g_attr_done = true;
   return IAM_OK;
+}
+
+template <int C>
+int launch_gdn_c(const GdnArgs& a, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_v_heads * C);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = sizeof(GdnSmem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (C > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = C;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  IAM_CUDA(cudaLaunchKernelEx(&cfg, gdn_fused_kernel<C>, a));
+  return IAM_OK;
+}
+
+// CTAs a head: the largest cluster (up to 8) that keeps every CTA of the
+// launch in one wave on the SMs; one CTA a head for a single token, where the
+// recurrence is one step and the split would only duplicate the q/k work.
+// IAM_GDN_SPLIT forces 1, 2, 4 or 8, for experiments.
+int gdn_split(int heads, int rows) {
+  if (const char* v = std::getenv("IAM_GDN_SPLIT")) {
+    const int c = std::atoi(v);
+    if (c == 1 || c == 2 || c == 4 || c == 8) return c;
+  }
+  if (rows < 4) return 1;
+  for (int c = 8; c > 1; c >>= 1)
+    if (heads * c <= g_sms) return c;
+  return 1;
 }
 
 int launch_gdn(const GdnArgs& a, cudaStream_t st, bool pdl) {
@@ -312,7 +421,16 @@ int launch_gdn(const GdnArgs& a, cudaStream_t st, bool pdl) {
             "gdn: 8-byte aligned rows required");
   const int r = ensure_attrs();
   if (r != IAM_OK) return r;
-  return launch_k(gdn_fused_kernel, dim3(a.n_v_heads), dim3(kThreads), sizeof(GdnSmem), st, pdl, a);
+  switch (gdn_split(a.n_v_heads, a.rows)) {
+    case 8:
+      return launch_gdn_c<8>(a, st, pdl);
+    case 4:
+      return launch_gdn_c<4>(a, st, pdl);
+    case 2:
+      return launch_gdn_c<2>(a, st, pdl);
+    default:
+      return launch_gdn_c<1>(a, st, pdl);
+  }
 }
 
 }  // namespace iam

@@ -188,9 +188,14 @@ def test_verify_equals_sequential_decode():
 
 
 # ---------------------------------------------------------------- recurrence drift
-def test_gdn_state_256_steps():
+@pytest.mark.parametrize("split", [None, "1", "2", "4", "8"])
+def test_gdn_state_256_steps(split, monkeypatch):
     """The fused GDN kernel over 256 tokens (8 verify blocks of 32) against the
-    oracle's per-token chain: fp32 state within 1e-4 relative."""
+    oracle's per-token chain: fp32 state within 1e-4 relative, outputs to the
+    parity bar, the conv window bit for bit; with the heads' state rows split
+    over 1, 2, 4 or 8 CTAs of a cluster (None: the library's choice)."""
+    if split is not None:
+        monkeypatch.setenv("IAM_GDN_SPLIT", split)
     d = O.QWEN35_27B
     rng = np.random.default_rng(256)
     C, HV, HK, VD = d.conv_dim, d.gdn_v_heads, d.gdn_k_heads, d.value_dim
@@ -232,3 +237,5 @@ def test_gdn_state_256_steps():
     assert rel_err(Sg, S) < 1e-4, rel_err(Sg, S)
     go = O.from_u16(host_u16(out))
     assert cosine(go, np.stack(outs)) > 0.9999
+    # the last block (7, odd) read cb and wrote the new window into ca
+    assert np.array_equal(host_u16(ca), O.to_u16(conv))
