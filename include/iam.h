@@ -252,6 +252,27 @@ const char* iam_engine_error(const iam_engine* e);
  * `bytes` must equal the full (unsharded) tensor size; each rank keeps its shard. */
 int iam_load_tensor(iam_engine* e, const char* name, const void* host_ptr, size_t bytes);
 
+/* Load every weight from the safetensors files of an MLX 4-bit checkpoint
+ * (its shards, in any order).  Replaces the reference's weight index + mmap +
+ * loadTensorToBuffer (full_forward.swift:451-472, 555-595), the per-layer
+ * tensor names (:749-822) and the lm_head load (:1279-1283).  Files are
+ * memory-mapped; each rank copies its shard through pinned staging buffers.
+ * Names may carry the "language_model." prefixes of multimodal exports;
+ * non-decoder tensors are ignored.  A 4-bit embedding (weight U32, scales
+ * and biases BF16) is dequantized once into the bf16 table with the
+ * reference's embed_lookup_bf16 arithmetic (:112-133); without lm_head.* the
+ * 4-bit embedding also serves as lm_head (tied).  Every engine tensor must be
+ * present with its dtype and size (A_log may be BF16), and no decoder tensor
+ * may be left over; otherwise IAM_EINVAL names the mismatches and nothing is
+ * loaded. */
+int iam_load_safetensors(iam_engine* e, const char* const* paths, int n_paths);
+
+/* The same matching without a GPU: checks that the files hold exactly the
+ * model `dims` describes and writes a summary (tensor count, bytes,
+ * embedding and lm_head forms, then one line per problem) into report. */
+int iam_check_safetensors(const iam_dims* dims, const char* const* paths, int n_paths, char* report,
+                          size_t report_len);
+
 /* Fill every weight with the seeded synthetic distributions of the benchmark
  * (generated on the GPU; bit-identical to oracle/synth.py). */
 int iam_init_synthetic(iam_engine* e, uint64_t seed);

@@ -25,6 +25,7 @@
 
 #include "kernels.cuh"
 #include "nccl_shim.h"
+#include "safetensors.h"
 #include "synth.cuh"
 
 namespace iam {
@@ -988,6 +989,313 @@ extern "C" int iam_load_tensor(iam_engine* eng, const char* name, const void* ho
   E_CUDA(cudaStreamSynchronize(e.stream));
   if (t.kind == Kind::kQ4Words || t.kind == Kind::kQ4Scales || t.kind == Kind::kQ4Biases) e.packed_dirty = true;
   return IAM_OK;
+}
+
+// ---------------------------------------------------------------- checkpoints
+namespace iam {
+namespace {
+
+const char* kind_dtype(Kind k) {
+  switch (k) {
+    case Kind::kQ4Words: return "U32";
+    case Kind::kF32: return "F32";
+    default: return "BF16";
+  }
+}
+
+// Where each of the engine's tensors comes from in a checkpoint.
+struct CkptPlan {
+  struct Item {
+    const TensorRec* t;
+    const StTensor* src;
+    bool to_f32;  // a bf16 tensor read into an fp32 one (A_log stored as bf16)
+  };
+  std::vector<Item> items;
+  bool embed_q4 = false;  // 4-bit embedding: dequantized into the bf16 table at load
+  const StTensor *ew = nullptr, *es = nullptr, *eb = nullptr;
+  bool tied = false;  // lm_head read from the 4-bit embedding
+  size_t bytes = 0;
+  std::vector<std::string> problems;
+};
+
+std::string shape_str(const std::vector<int64_t>& s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); ++i) r += (i ? ", " : "") + std::to_string(s[i]);
+  return r + "]";
+}
+
+void plan_checkpoint(const EngineImpl& e, const StCheckpoint& ck, CkptPlan& plan) {
+  auto find = [&](const std::string& n) -> const StTensor* {
+    auto it = ck.tensors.find(n);
+    return it == ck.tensors.end() ? nullptr : &it->second;
+  };
+  // embedding: a bf16 table, or the reference's 4-bit one (embed_lookup_bf16,
+  // full_forward.swift:112-133) dequantized once into the table
+  const int64_t V = e.d.vocab, H = e.d.hidden, G = H / e.d.group_size;
+  if (const StTensor* w = find("model.embed_tokens.weight")) {
+    if (w->dtype == "U32") {
+      plan.ew = w;
+      plan.es = find("model.embed_tokens.scales");
+      plan.eb = find("model.embed_tokens.biases");
+      const size_t wb = static_cast<size_t>(V * H / 2), sb = static_cast<size_t>(V * G * 2);
+      if (w->bytes() != wb || !plan.es || !plan.eb || plan.es->dtype != "BF16" || plan.eb->dtype != "BF16" ||
+          plan.es->bytes() != sb || plan.eb->bytes() != sb)
+        plan.problems.push_back("model.embed_tokens: a 4-bit embedding needs weight U32 [" + std::to_string(V) + ", " +
+                                std::to_string(H / 8) + "] with BF16 scales and biases [" + std::to_string(V) + ", " +
+                                std::to_string(G) + "]");
+      else
+        plan.embed_q4 = true;
+    }
+  }
+  for (const TensorRec& t : e.tensors) {
+    const size_t full = static_cast<size_t>(t.full_rows) * t.full_cols * t.esize;
+    if (t.name == "model.embed_tokens.weight" && plan.embed_q4) {
+      plan.bytes += plan.ew->bytes() + plan.es->bytes() + plan.eb->bytes();
+      continue;
+    }
+    const StTensor* src = find(t.name);
+    if (!src && t.name.compare(0, 8, "lm_head.") == 0 && plan.embed_q4) {
+      src = find("model.embed_tokens." + t.name.substr(8));  // tied output embedding
+      if (src) plan.tied = true;
+    }
+    if (!src) {
+      plan.problems.push_back("missing " + t.name);
+      continue;
+    }
+    bool to_f32 = false;
+    if (src->dtype != kind_dtype(t.kind)) {
+      if (t.kind == Kind::kF32 && src->dtype == "BF16" && src->bytes() * 2 == full) {
+        to_f32 = true;
+      } else {
+        plan.problems.push_back(t.name + ": dtype " + src->dtype + ", expected " + kind_dtype(t.kind));
+        continue;
+      }
+    }
+    if (!to_f32 && src->bytes() != full) {
+      plan.problems.push_back(t.name + ": shape " + shape_str(src->shape) + " " + src->dtype + " (" +
+                              std::to_string(src->bytes()) + " bytes), expected [" + std::to_string(t.full_rows) +
+                              ", " + std::to_string(t.full_cols) + "] (" + std::to_string(full) + " bytes)");
+      continue;
+    }
+    if (t.full_rows > 1 && src->shape.size() >= 2 && src->shape[0] != t.full_rows) {
+      plan.problems.push_back(t.name + ": shape " + shape_str(src->shape) + ", expected " +
+                              std::to_string(t.full_rows) + " rows");
+      continue;
+    }
+    plan.items.push_back({&t, src, to_f32});
+    plan.bytes += src->bytes();
+  }
+  // decoder tensors the engine has no place for: a different architecture
+  for (const auto& kv : ck.tensors) {
+    if (e.by_name.count(kv.first)) continue;
+    if (plan.embed_q4 && (kv.first == "model.embed_tokens.scales" || kv.first == "model.embed_tokens.biases")) continue;
+    plan.problems.push_back("unused tensor " + kv.second.name);
+  }
+}
+
+// Host -> device copies staged through two pinned buffers: the gather from
+// the mapped file into one overlaps the DMA out of the other.
+struct Staging {
+  static constexpr size_t kBytes = 32u << 20;
+  unsigned char* buf[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  bool used[2] = {false, false};
+  int next = 0;
+  cudaStream_t st = nullptr;
+  ~Staging() {
+    if (st) cudaStreamSynchronize(st);
+    for (int i = 0; i < 2; ++i) {
+      if (buf[i]) cudaFreeHost(buf[i]);
+      if (ev[i]) cudaEventDestroy(ev[i]);
+    }
+  }
+  cudaError_t init(cudaStream_t s) {
+    st = s;
+    for (int i = 0; i < 2; ++i) {
+      cudaError_t r = cudaHostAlloc(reinterpret_cast<void**>(&buf[i]), kBytes, cudaHostAllocDefault);
+      if (r != cudaSuccess) return r;
+      r = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+      if (r != cudaSuccess) return r;
+    }
+    return cudaSuccess;
+  }
+  // the next free buffer
+  cudaError_t take(unsigned char** out) {
+    const int b = next;
+    next ^= 1;
+    if (used[b]) {
+      const cudaError_t r = cudaEventSynchronize(ev[b]);
+      if (r != cudaSuccess) return r;
+    }
+    used[b] = true;
+    *out = buf[b];
+    cur = b;
+    return cudaSuccess;
+  }
+  cudaError_t send(void* dst, size_t n) {
+    cudaError_t r = cudaMemcpyAsync(dst, buf[cur], n, cudaMemcpyHostToDevice, st);
+    if (r == cudaSuccess) r = cudaEventRecord(ev[cur], st);
+    return r;
+  }
+  int cur = 0;
+};
+
+// rows [r0, r1) x columns [c0, c1) (bytes) of a row-major host matrix with
+// `pitch` bytes a row, to contiguous device memory at dst
+int stage_rows(EngineImpl& e, Staging& sg, const unsigned char* src, size_t pitch, int64_t r0, int64_t r1, size_t c0,
+               size_t width, unsigned char* dst) {
+  const int64_t per = std::max<int64_t>(1, static_cast<int64_t>(Staging::kBytes / width));
+  for (int64_t r = r0; r < r1; r += per) {
+    const int64_t n = std::min(per, r1 - r);
+    unsigned char* b = nullptr;
+    E_CUDA(sg.take(&b));
+    if (width == pitch) {
+      std::memcpy(b, src + r * pitch, static_cast<size_t>(n) * pitch);
+    } else {
+      for (int64_t i = 0; i < n; ++i) std::memcpy(b + i * width, src + (r + i) * pitch + c0, width);
+    }
+    E_CUDA(sg.send(dst, static_cast<size_t>(n) * width));
+    dst += static_cast<size_t>(n) * width;
+  }
+  return IAM_OK;
+}
+
+// one tensor's shard, as iam_load_tensor places it
+int stage_tensor(EngineImpl& e, Staging& sg, const TensorRec& t, const unsigned char* src) {
+  unsigned char* dst = static_cast<unsigned char*>(t.ptr);
+  const size_t width = static_cast<size_t>(t.shard.col1 - t.shard.col0) * t.esize;
+  const size_t pitch = static_cast<size_t>(t.full_cols) * t.esize;
+  for (auto& rr : t.shard.rows) {
+    E_RUN(stage_rows(e, sg, src, pitch, rr.first, rr.second, static_cast<size_t>(t.shard.col0) * t.esize, width, dst));
+    dst += static_cast<size_t>(rr.second - rr.first) * width;
+  }
+  return IAM_OK;
+}
+
+int load_checkpoint(EngineImpl& e, const StCheckpoint& ck, const CkptPlan& plan) {
+  E_CUDA(cudaSetDevice(e.device));
+  Staging sg;
+  E_CUDA(sg.init(e.stream));
+  for (const auto& it : plan.items) {
+    const unsigned char* src = static_cast<const unsigned char*>(ck.data(*it.src));
+    if (!it.to_f32) {
+      E_RUN(stage_tensor(e, sg, *it.t, src));
+      continue;
+    }
+    const size_t n = it.src->bytes() / 2;
+    std::vector<float> f(n);
+    for (size_t i = 0; i < n; ++i) {
+      uint16_t h;
+      std::memcpy(&h, src + 2 * i, 2);
+      const uint32_t u = static_cast<uint32_t>(h) << 16;
+      std::memcpy(&f[i], &u, 4);
+    }
+    E_RUN(stage_tensor(e, sg, *it.t, reinterpret_cast<const unsigned char*>(f.data())));
+    E_CUDA(cudaStreamSynchronize(e.stream));  // f is released below
+  }
+  if (plan.embed_q4) {
+    // the 4-bit table through device scratch, a block of rows at a time,
+    // dequantized by the reference's embed_lookup_bf16 arithmetic
+    const int64_t V = e.d.vocab, H = e.d.hidden, G = H / e.d.group_size;
+    const int64_t rows = 8192;
+    struct Tmp {
+      void* p[4] = {nullptr, nullptr, nullptr, nullptr};
+      ~Tmp() {
+        for (void* q : p)
+          if (q) cudaFree(q);
+      }
+    } tmp;
+    E_CUDA(cudaMalloc(&tmp.p[0], static_cast<size_t>(rows * H / 2)));
+    E_CUDA(cudaMalloc(&tmp.p[1], static_cast<size_t>(rows * G * 2)));
+    E_CUDA(cudaMalloc(&tmp.p[2], static_cast<size_t>(rows * G * 2)));
+    E_CUDA(cudaMalloc(&tmp.p[3], static_cast<size_t>(rows * 4)));
+    std::vector<int32_t> ids(static_cast<size_t>(rows));
+    for (int64_t i = 0; i < rows; ++i) ids[static_cast<size_t>(i)] = static_cast<int32_t>(i);
+    E_CUDA(cudaMemcpy(tmp.p[3], ids.data(), ids.size() * 4, cudaMemcpyHostToDevice));
+    const unsigned char* w = static_cast<const unsigned char*>(ck.data(*plan.ew));
+    const unsigned char* sc = static_cast<const unsigned char*>(ck.data(*plan.es));
+    const unsigned char* bi = static_cast<const unsigned char*>(ck.data(*plan.eb));
+    for (int64_t r = 0; r < V; r += rows) {
+      const int64_t n = std::min(rows, V - r);
+      E_RUN(stage_rows(e, sg, w, H / 2, r, r + n, 0, H / 2, static_cast<unsigned char*>(tmp.p[0])));
+      E_RUN(stage_rows(e, sg, sc, G * 2, r, r + n, 0, G * 2, static_cast<unsigned char*>(tmp.p[1])));
+      E_RUN(stage_rows(e, sg, bi, G * 2, r, r + n, 0, G * 2, static_cast<unsigned char*>(tmp.p[2])));
+      const int rc = iam_embed_lookup_q4(static_cast<const uint32_t*>(tmp.p[0]), static_cast<const uint16_t*>(tmp.p[1]),
+                                         static_cast<const uint16_t*>(tmp.p[2]), static_cast<const int32_t*>(tmp.p[3]),
+                                         e.embed + static_cast<size_t>(r) * H, static_cast<int>(n), static_cast<int>(H),
+                                         e.d.group_size, e.stream);
+      if (rc != IAM_OK) return e.setf(rc, iam_last_error());
+      E_CUDA(cudaStreamSynchronize(e.stream));  // the scratch is reused by the next block
+    }
+  }
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  e.packed_dirty = true;
+  return IAM_OK;
+}
+
+std::vector<std::string> path_list(const char* const* paths, int n) {
+  std::vector<std::string> v;
+  for (int i = 0; i < n; ++i) v.push_back(paths[i] ? paths[i] : "");
+  return v;
+}
+
+std::string plan_summary(const CkptPlan& plan, const StCheckpoint& ck) {
+  std::string r = std::to_string(plan.items.size() + (plan.embed_q4 ? 1 : 0)) + " tensors, " +
+                  std::to_string(plan.bytes) + " bytes from " + std::to_string(ck.files.size()) + " file(s); embedding " +
+                  (plan.embed_q4 ? "4-bit (dequantized at load)" : "bf16") + "; lm_head " +
+                  (plan.tied ? "tied to the embedding" : "own") + "; " + std::to_string(ck.ignored.size()) +
+                  " non-decoder tensors ignored";
+  for (const auto& p : plan.problems) r += "\n" + p;
+  return r;
+}
+
+}  // namespace
+}  // namespace iam
+
+extern "C" int iam_check_safetensors(const iam_dims* dims, const char* const* paths, int n_paths, char* report,
+                                     size_t report_len) {
+  using namespace iam;
+  IAM_CHECK(dims && paths && n_paths > 0, "iam_check_safetensors: bad arguments");
+  int r = validate_dims(*dims, 1);
+  if (r != IAM_OK) return r;
+  EngineImpl e;
+  e.d = *dims;
+  r = build_registry(e);
+  if (r != IAM_OK) return fail(r, e.err);
+  StCheckpoint ck;
+  std::string err;
+  std::string text;
+  CkptPlan plan;
+  if (!st_open(path_list(paths, n_paths), ck, err)) {
+    text = err;
+    r = fail(IAM_EINVAL, err);
+  } else {
+    plan_checkpoint(e, ck, plan);
+    text = plan_summary(plan, ck);
+    r = plan.problems.empty() ? IAM_OK : fail(IAM_EINVAL, "checkpoint: " + plan.problems.front());
+  }
+  if (report && report_len) {
+    std::strncpy(report, text.c_str(), report_len - 1);
+    report[report_len - 1] = '\0';
+  }
+  return r;
+}
+
+extern "C" int iam_load_safetensors(iam_engine* eng, const char* const* paths, int n_paths) {
+  using namespace iam;
+  IAM_CHECK(eng && paths && n_paths > 0, "iam_load_safetensors: bad arguments");
+  EngineImpl& e = eng->impl;
+  StCheckpoint ck;
+  std::string err;
+  if (!st_open(path_list(paths, n_paths), ck, err)) return e.setf(IAM_EINVAL, err);
+  CkptPlan plan;
+  plan_checkpoint(e, ck, plan);
+  if (!plan.problems.empty()) {
+    std::string m = "checkpoint does not match the model (" + std::to_string(plan.problems.size()) + " problems):";
+    for (size_t i = 0; i < plan.problems.size() && i < 8; ++i) m += "\n  " + plan.problems[i];
+    return e.setf(IAM_EINVAL, m);
+  }
+  return load_checkpoint(e, ck, plan);
 }
 
 extern "C" int iam_read_tensor(iam_engine* eng, const char* name, void* host_ptr, size_t bytes) {

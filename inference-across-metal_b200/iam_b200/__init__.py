@@ -54,6 +54,8 @@ _SIGS = {
     "iam_destroy": (None, [_vp]),
     "iam_engine_error": (C.c_char_p, [_vp]),
     "iam_load_tensor": (_i, [_vp, _cp, _vp, _sz]),
+    "iam_load_safetensors": (_i, [_vp, _vp, _i]),
+    "iam_check_safetensors": (_i, [_vp, _vp, _i, _vp, _sz]),
     "iam_init_synthetic": (_i, [_vp, _u64]),
     "iam_state_init": (_i, [_vp, _u64, _i]),
     "iam_state_reset": (_i, [_vp]),
@@ -226,6 +228,14 @@ def tp_shard_of(dims: Dims, rank: int, world: int) -> TpShard:
     return out
 
 
+def check_safetensors(dims: Dims, paths):
+    """(status, report): do the files hold exactly the model `dims` describes? (host only)"""
+    arr = (C.c_char_p * len(paths))(*[os.fsencode(p) for p in paths])
+    buf = C.create_string_buffer(1 << 16)
+    st = lib().iam_check_safetensors(C.byref(dims), arr, len(paths), buf, len(buf))
+    return st, buf.value.decode()
+
+
 def nccl_unique_id() -> bytes:
     buf = C.create_string_buffer(128)
     _check(lib().iam_nccl_unique_id(buf))
@@ -260,6 +270,11 @@ class Engine:
         import numpy as np
         a = np.ascontiguousarray(host_array)
         self._c(lib().iam_load_tensor(self._h, name.encode(), a.ctypes.data_as(C.c_void_p), a.nbytes))
+
+    def load_safetensors(self, paths):
+        """Load every weight from the safetensors files of an MLX 4-bit checkpoint."""
+        arr = (C.c_char_p * len(paths))(*[os.fsencode(p) for p in paths])
+        self._c(lib().iam_load_safetensors(self._h, arr, len(paths)))
 
     def init_synthetic(self, seed: int):
         self._c(lib().iam_init_synthetic(self._h, seed))
