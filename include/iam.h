@@ -291,6 +291,18 @@ int iam_state_reset(iam_engine* e);
 int iam_verify(iam_engine* e, const int32_t* tokens, int K, int pos, int32_t* argmax_out, int* accept_len);
 int iam_decode_step(iam_engine* e, int32_t token, int pos, int32_t* next_token);
 
+/* Greedy generation (runTest, test_context.swift:1216-1270; forwardPass per
+ * token, full_forward.swift:1198-1308): resets the state, runs the prompt at
+ * positions 0..n_prompt-1 in verify blocks of up to max_rows tokens (the same
+ * result as one token at a time), takes the last position's argmax as the
+ * first generated token, then decodes one token at a time until max_new
+ * tokens are out or one of the n_eos stop ids (Qwen3.5: 248046 <|im_end|>,
+ * 248044 <|endoftext|>, warm_forward.swift:1254-1256) was emitted; the stop
+ * id is kept.  out: int32 [max_new]; *n_out: tokens written.  Requires
+ * n_prompt + max_new - 1 <= max_ctx. */
+int iam_generate(iam_engine* e, const int32_t* prompt, int n_prompt, int max_new, const int32_t* eos, int n_eos,
+                 int32_t* out, int* n_out);
+
 /* Device-resident variant for benchmarking: tokens/outputs stay on the GPU
  * (d_tokens int32 [K], d_argmax int32 [K]) and nothing is synchronised. */
 int iam_verify_device(iam_engine* e, const int32_t* d_tokens, int K, int pos, int32_t* d_argmax, void* stream);

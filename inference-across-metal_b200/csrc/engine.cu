@@ -1472,6 +1472,41 @@ extern "C" int iam_decode_step(iam_engine* eng, int32_t token, int pos, int32_t*
   return iam_verify(eng, &token, 1, pos, next_token, &acc);
 }
 
+extern "C" int iam_generate(iam_engine* eng, const int32_t* prompt, int n_prompt, int max_new, const int32_t* eos,
+                            int n_eos, int32_t* out, int* n_out) {
+  using namespace iam;
+  IAM_CHECK(eng && prompt && out && n_out && n_prompt > 0 && max_new > 0 && n_eos >= 0 && (eos || n_eos == 0),
+            "iam_generate: bad arguments");
+  EngineImpl& e = eng->impl;
+  *n_out = 0;
+  if (n_prompt + max_new - 1 > e.d.max_ctx)
+    return e.setf(IAM_EINVAL, "iam_generate: prompt + max_new - 1 exceeds max_ctx");
+  auto is_eos = [&](int32_t t) {
+    for (int i = 0; i < n_eos; ++i)
+      if (eos[i] == t) return true;
+    return false;
+  };
+  // runTest (test_context.swift:1216-1270): reset, prefill, then greedy steps
+  int r = iam_state_reset(eng);
+  if (r != IAM_OK) return r;
+  std::vector<int32_t> am(static_cast<size_t>(e.d.max_rows));
+  int32_t next = -1;
+  for (int p0 = 0; p0 < n_prompt; p0 += e.d.max_rows) {  // prefill in verify blocks
+    const int k = std::min(e.d.max_rows, n_prompt - p0);
+    r = iam_verify(eng, prompt + p0, k, p0, am.data(), nullptr);
+    if (r != IAM_OK) return r;
+    next = am[static_cast<size_t>(k - 1)];
+  }
+  int pos = n_prompt;
+  out[(*n_out)++] = next;
+  while (*n_out < max_new && !is_eos(next)) {
+    r = iam_decode_step(eng, next, pos++, &next);
+    if (r != IAM_OK) return r;
+    out[(*n_out)++] = next;
+  }
+  return IAM_OK;
+}
+
 extern "C" int iam_verify_device(iam_engine* eng, const int32_t* d_tokens, int K, int pos, int32_t* d_argmax,
                                  void* stream) {
   using namespace iam;

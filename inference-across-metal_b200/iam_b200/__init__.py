@@ -61,6 +61,7 @@ _SIGS = {
     "iam_state_reset": (_i, [_vp]),
     "iam_verify": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "iam_decode_step": (_i, [_vp, C.c_int32, _i, _vp]),
+    "iam_generate": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp, _vp]),
     "iam_verify_device": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "iam_read_tensor": (_i, [_vp, _cp, _vp, _sz]),
     "iam_read_hidden": (_i, [_vp, _vp, _i]),
@@ -293,6 +294,18 @@ class Engine:
         self._c(lib().iam_verify(self._h, t.ctypes.data_as(C.c_void_p), len(t), pos,
                                  out.ctypes.data_as(C.c_void_p), C.byref(acc)))
         return out, acc.value
+
+    def generate(self, prompt, max_new: int, eos=(248046, 248044)):
+        """Greedy generation from a reset state; returns the generated token ids."""
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        e = np.ascontiguousarray(list(eos), dtype=np.int32)
+        out = np.zeros(max_new, np.int32)
+        n = C.c_int(0)
+        self._c(lib().iam_generate(self._h, p.ctypes.data_as(C.c_void_p), len(p), max_new,
+                                   e.ctypes.data_as(C.c_void_p), len(e), out.ctypes.data_as(C.c_void_p),
+                                   C.byref(n)))
+        return out[:n.value]
 
     def verify_device(self, d_tokens, K: int, pos: int, d_argmax=None, stream=None):
         self._c(lib().iam_verify_device(self._h, d_tokens, K, pos, d_argmax, _s(stream)))
