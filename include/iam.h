@@ -291,6 +291,24 @@ int iam_state_reset(iam_engine* e);
 int iam_verify(iam_engine* e, const int32_t* tokens, int K, int pos, int32_t* argmax_out, int* accept_len);
 int iam_decode_step(iam_engine* e, int32_t token, int pos, int32_t* next_token);
 
+/* Speculative-decode rollback: keep the recurrent state after the first
+ * n_keep tokens of the last verify block (1 <= n_keep <= its K), as if only
+ * those tokens had been verified.  After a verify that returned accept_len
+ * j, tokens[0..j] are the accepted ones: call iam_rollback(e, j + 1, ...) and
+ * start the next block at pos + j + 1 with argmax_out[j].  Every step keeps
+ * the state it started from; the GDN recurrence of the kept rows is re-run
+ * from it (conv windows included) and the device position moves back to
+ * pos + n_keep.  KV-cache rows of rejected tokens need no undo (the next
+ * block writes them before any query reads them).  n_keep == K re-runs the
+ * block and leaves the state as the step left it.  Enqueued on `stream`
+ * (NULL: the engine's own stream), which must be the stream the verify ran
+ * on; IAM_ESTATE when no verify ran since the state was last set.  Tensor
+ * parallel engines: every rank calls it with the same n_keep (no collective).
+ * No counterpart in the reference: its verify loop (batch_verify_27b.swift:
+ * 141-274) never commits a partial block, and the GDN conv state flips
+ * (full_forward.swift:1196, 1259) are the only state it swaps. */
+int iam_rollback(iam_engine* e, int n_keep, void* stream);
+
 /* Greedy generation (runTest, test_context.swift:1216-1270; forwardPass per
  * token, full_forward.swift:1198-1308): resets the state, runs the prompt at
  * positions 0..n_prompt-1 in verify blocks of up to max_rows tokens (the same

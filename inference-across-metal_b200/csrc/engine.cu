@@ -133,18 +133,24 @@ struct EngineImpl {
   uint16_t* final_norm = nullptr;
   QW lm;
 
-  // state
+  // state; S holds two copies of every GDN layer's state (s_half floats
+  // apart) and conv two windows, swapped each step by *d_parity: a step reads
+  // the state before it and leaves that copy intact, which is what
+  // iam_rollback replays the accepted rows from
   float* S = nullptr;
+  size_t s_half = 0;
   uint16_t* conv[2] = {nullptr, nullptr};
   uint16_t* kc = nullptr;
   uint16_t* vc = nullptr;
   int* d_parity = nullptr;
   int parity = 0;
+  int last_K = 0;  // rows of the last verify block since the state was set (0: none to roll back)
 
   // activations / workspace
   int ld_in = 0, ld_attn = 0;
   uint16_t *hidden = nullptr, *resid = nullptr, *normed = nullptr, *inproj = nullptr, *mid = nullptr,
            *mlp_h = nullptr, *q_buf = nullptr;
+  uint16_t* gin = nullptr;  // [n_gdn][max_rows][ld_in]: each GDN layer's projections of the last block
   float *part_o = nullptr, *part_ml = nullptr, *red32 = nullptr;
   float* qws = nullptr;  // split-K workspace of the matmuls (zero between launches)
   int* qctr = nullptr;
@@ -401,7 +407,8 @@ int alloc_all(EngineImpl& e) {
 
   // state
   const size_t s_per = static_cast<size_t>(e.gv_l) * d.gdn_dk * d.gdn_dv;
-  E_CUDA(cudaMalloc(&e.S, std::max<size_t>(1, e.n_gdn * s_per) * sizeof(float)));
+  e.s_half = static_cast<size_t>(e.n_gdn) * s_per;
+  E_CUDA(cudaMalloc(&e.S, std::max<size_t>(1, 2 * e.s_half) * sizeof(float)));
   for (int i = 0; i < 2; ++i)
     E_CUDA(cudaMalloc(&e.conv[i], std::max<size_t>(1, static_cast<size_t>(e.n_gdn) * 3 * e.conv_l) * 2));
   const size_t kv = static_cast<size_t>(e.n_attn) * d.max_ctx * e.hkv_l * d.head_dim;
@@ -420,6 +427,7 @@ int alloc_all(EngineImpl& e) {
   E_CUDA(cudaMalloc(&e.resid, static_cast<size_t>(R) * H * 2));
   E_CUDA(cudaMalloc(&e.normed, static_cast<size_t>(R) * H * 2));
   E_CUDA(cudaMalloc(&e.inproj, static_cast<size_t>(R) * ld_big * 2));
+  E_CUDA(cudaMalloc(&e.gin, std::max<size_t>(1, static_cast<size_t>(e.n_gdn) * R * e.ld_in) * 2));
   E_CUDA(cudaMalloc(&e.mid, static_cast<size_t>(R) * ld_mid * 2));
   E_CUDA(cudaMalloc(&e.mlp_h, static_cast<size_t>(R) * e.inter_l * 2));
   E_CUDA(cudaMalloc(&e.q_buf, static_cast<size_t>(R) * e.hq_l * d.head_dim * 2));
@@ -538,32 +546,13 @@ int run_qmm(EngineImpl& e, QmmArgs& a, const char* kind, double bytes) {
 // GPU; fp32 partials + NCCL all-reduce + residual kernel across GPUs.
 int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, const uint16_t* resid, uint16_t* out);
 
-int enqueue_gdn(EngineImpl& e, const Layer& L, int K) {
+// The GDN kernel's arguments for layer L over the first `rows` rows of the
+// layer's projections of the current block (e.gin); the state buffers and
+// conv windows are picked on the device by *d_parity.
+GdnArgs gdn_args(EngineImpl& e, const Layer& L, int rows) {
   const iam_dims& d = e.d;
-  const int H = d.hidden;
-  {
-    Recorder rec(e, "rmsnorm", 4.0 * K * H);
-    E_RUN(launch_rms_norm(e.hidden, H, L.in_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
-  }
-  QmmArgs a = {};
-  a.x = e.normed;
-  a.ldx = H;
-  a.M = K;
-  a.K = H;
-  a.nseg = 4;
-  seg_of(a.seg[0], L.qkv, EPI_STORE);
-  a.seg[0].out = e.inproj;
-  seg_of(a.seg[1], L.z, EPI_STORE);
-  a.seg[1].out = e.inproj + e.conv_l;
-  seg_of(a.seg[2], L.bproj, EPI_STORE);
-  a.seg[2].out = e.inproj + e.conv_l + e.vd_l;
-  seg_of(a.seg[3], L.aproj, EPI_STORE);
-  a.seg[3].out = e.inproj + e.conv_l + e.vd_l + e.gv_l;
-  for (int i = 0; i < 4; ++i) a.seg[i].ldo = e.ld_in;
-  E_RUN(run_qmm(e, a, "qmm", qbytes(L.qkv) + qbytes(L.z) + qbytes(L.bproj) + qbytes(L.aproj)));
-
   GdnArgs g = {};
-  g.in = e.inproj;
+  g.in = e.gin + static_cast<size_t>(L.idx) * d.max_rows * e.ld_in;
   g.ld_in = e.ld_in;
   g.z_col = e.conv_l;
   g.b_col = e.conv_l + e.vd_l;
@@ -577,14 +566,44 @@ int enqueue_gdn(EngineImpl& e, const Layer& L, int K) {
   g.dt_bias = L.dt_bias;
   g.norm_w = L.norm_w;
   g.S = e.S + static_cast<size_t>(L.idx) * e.gv_l * d.gdn_dk * d.gdn_dv;
+  g.S_alt = g.S + e.s_half;
   g.out = e.mid;
   g.ld_out = e.vd_l;
   g.n_k_heads = e.gk_l;
   g.n_v_heads = e.gv_l;
   g.key_dim = e.key_l;
   g.conv_dim = e.conv_l;
-  g.rows = K;
+  g.rows = rows;
   g.eps = d.eps;
+  return g;
+}
+
+int enqueue_gdn(EngineImpl& e, const Layer& L, int K) {
+  const iam_dims& d = e.d;
+  const int H = d.hidden;
+  uint16_t* const in = e.gin + static_cast<size_t>(L.idx) * d.max_rows * e.ld_in;
+  {
+    Recorder rec(e, "rmsnorm", 4.0 * K * H);
+    E_RUN(launch_rms_norm(e.hidden, H, L.in_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
+  }
+  QmmArgs a = {};
+  a.x = e.normed;
+  a.ldx = H;
+  a.M = K;
+  a.K = H;
+  a.nseg = 4;
+  seg_of(a.seg[0], L.qkv, EPI_STORE);
+  a.seg[0].out = in;
+  seg_of(a.seg[1], L.z, EPI_STORE);
+  a.seg[1].out = in + e.conv_l;
+  seg_of(a.seg[2], L.bproj, EPI_STORE);
+  a.seg[2].out = in + e.conv_l + e.vd_l;
+  seg_of(a.seg[3], L.aproj, EPI_STORE);
+  a.seg[3].out = in + e.conv_l + e.vd_l + e.gv_l;
+  for (int i = 0; i < 4; ++i) a.seg[i].ldo = e.ld_in;
+  E_RUN(run_qmm(e, a, "qmm", qbytes(L.qkv) + qbytes(L.z) + qbytes(L.bproj) + qbytes(L.aproj)));
+
+  const GdnArgs g = gdn_args(e, L, K);
   {
     Recorder rec(e, "gdn", 2.0 * e.gv_l * d.gdn_dk * d.gdn_dv * 4 + 2.0 * 3 * e.conv_l * 2);
     E_RUN(launch_gdn(g, e.stream, e.pdl));
@@ -692,6 +711,29 @@ __global__ void resid_from_f32_kernel(const float* y, const uint16_t* resid, uin
 __global__ void advance_kernel(StepIn* in, int* parity, int K) {
   in->pos += K;
   *parity ^= 1;
+}
+
+// Undoes advance_kernel: the state copies the last step read become the
+// current ones again and the device position returns to the block's start.
+__global__ void rewind_kernel(StepIn* in, int* parity, int K) {
+  in->pos -= K;
+  *parity ^= 1;
+}
+
+// Re-runs the GDN recurrence of every GDN layer over the first n_keep rows of
+// the last block, from the state copies that block read, into the copies it
+// wrote; the device position ends n_keep past the block's start.  The
+// attention layers need nothing: the KV-cache rows of rejected tokens lie past
+// the new position, and the next block overwrites them before any query
+// reaches them (a query at position p reads rows <= p).
+int enqueue_rollback(EngineImpl& e, int K, int n_keep, cudaStream_t st) {
+  rewind_kernel<<<1, 1, 0, st>>>(e.d_in, e.d_parity, K);
+  E_CUDA(cudaGetLastError());
+  for (const Layer& L : e.layers)
+    if (!L.attn) E_RUN(launch_gdn(gdn_args(e, L, n_keep), st, false));
+  advance_kernel<<<1, 1, 0, st>>>(e.d_in, e.d_parity, n_keep);
+  E_CUDA(cudaGetLastError());
+  return IAM_OK;
 }
 
 
@@ -954,7 +996,7 @@ extern "C" void iam_destroy(iam_engine* eng) {
   if (e.comm) iam::nccl_destroy(e.comm);
   void* bufs[] = {e.pool, e.ppool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
                   e.mid, e.mlp_h, e.q_buf, e.part_o, e.part_ml, e.red32, e.keys, e.best, e.rope_cs, e.d_in, e.d_out,
-                  e.d_err, e.qws, e.qctr};
+                  e.d_err, e.qws, e.qctr, e.gin};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (e.h_in) cudaFreeHost(e.h_in);
@@ -1317,8 +1359,10 @@ extern "C" int iam_read_tensor(iam_engine* eng, const char* name, void* host_ptr
     if (li < 0 || li >= e.d.n_layers) return e.setf(IAM_EINVAL, "iam_read_tensor: layer out of range");
     const Layer& L = e.layers[li];
     if (n.rfind("state.S.", 0) == 0 && !L.attn) {
+      int par = 0;
+      E_CUDA(cudaMemcpy(&par, e.d_parity, sizeof(int), cudaMemcpyDeviceToHost));
       have = static_cast<size_t>(e.gv_l) * e.d.gdn_dk * e.d.gdn_dv * 4;
-      src = e.S + static_cast<size_t>(L.idx) * e.gv_l * e.d.gdn_dk * e.d.gdn_dv;
+      src = e.S + (par ? e.s_half : 0) + static_cast<size_t>(L.idx) * e.gv_l * e.d.gdn_dk * e.d.gdn_dv;
     } else if (n.rfind("state.conv.", 0) == 0 && !L.attn) {
       int par = 0;
       E_CUDA(cudaMemcpy(&par, e.d_parity, sizeof(int), cudaMemcpyDeviceToHost));
@@ -1352,8 +1396,7 @@ extern "C" int iam_state_reset(iam_engine* eng) {
   IAM_CHECK(eng, "iam_state_reset: null engine");
   EngineImpl& e = eng->impl;
   E_CUDA(cudaSetDevice(e.device));
-  const size_t s = static_cast<size_t>(e.n_gdn) * e.gv_l * e.d.gdn_dk * e.d.gdn_dv * 4;
-  if (s) E_CUDA(cudaMemsetAsync(e.S, 0, s, e.stream));
+  if (e.s_half) E_CUDA(cudaMemsetAsync(e.S, 0, 2 * e.s_half * sizeof(float), e.stream));
   for (int i = 0; i < 2; ++i)
     if (e.n_gdn) E_CUDA(cudaMemsetAsync(e.conv[i], 0, static_cast<size_t>(e.n_gdn) * 3 * e.conv_l * 2, e.stream));
   const size_t kv = static_cast<size_t>(e.n_attn) * e.d.max_ctx * e.hkv_l * e.d.head_dim * 2;
@@ -1363,6 +1406,7 @@ extern "C" int iam_state_reset(iam_engine* eng) {
   }
   E_CUDA(cudaMemsetAsync(e.d_parity, 0, sizeof(int), e.stream));
   E_CUDA(cudaStreamSynchronize(e.stream));
+  e.last_K = 0;
   return IAM_OK;
 }
 
@@ -1460,6 +1504,7 @@ extern "C" int iam_verify(iam_engine* eng, const int32_t* tokens, int K, int pos
   std::memcpy(e.h_in->tokens, tokens, sizeof(int32_t) * K);
   E_CUDA(cudaMemcpyAsync(e.d_in, e.h_in, sizeof(int32_t) * (1 + K), cudaMemcpyHostToDevice, e.stream));
   E_CUDA(cudaGraphLaunch(g, e.stream));
+  e.last_K = K;
   E_CUDA(cudaMemcpyAsync(e.h_out, e.d_out, sizeof(int32_t) * (1 + K), cudaMemcpyDeviceToHost, e.stream));
   E_CUDA(cudaStreamSynchronize(e.stream));
   std::memcpy(argmax_out, e.h_out + 1, sizeof(int32_t) * K);
@@ -1527,7 +1572,24 @@ extern "C" int iam_verify_device(iam_engine* eng, const int32_t* d_tokens, int K
   }
   if (d_tokens) E_CUDA(cudaMemcpyAsync(e.d_in->tokens, d_tokens, sizeof(int32_t) * K, cudaMemcpyDeviceToDevice, st));
   E_CUDA(cudaGraphLaunch(g, st));
+  e.last_K = K;
   if (d_argmax) E_CUDA(cudaMemcpyAsync(d_argmax, e.d_out + 1, sizeof(int32_t) * K, cudaMemcpyDeviceToDevice, st));
+  return IAM_OK;
+}
+
+extern "C" int iam_rollback(iam_engine* eng, int n_keep, void* stream) {
+  using namespace iam;
+  IAM_CHECK(eng, "iam_rollback: null engine");
+  EngineImpl& e = eng->impl;
+  if (e.last_K == 0)
+    return e.setf(IAM_ESTATE, "iam_rollback: no verify block since the state was reset or initialised");
+  if (n_keep < 1 || n_keep > e.last_K)
+    return e.setf(IAM_EINVAL, "iam_rollback: n_keep out of range (1..rows of the last verify)");
+  E_CUDA(cudaSetDevice(e.device));
+  const int K = e.last_K;
+  E_RUN(enqueue_rollback(e, K, n_keep, stream ? as_stream(stream) : e.stream));
+  e.host_pos += n_keep - K;
+  e.last_K = n_keep;
   return IAM_OK;
 }
 

@@ -167,15 +167,21 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rep = a.n_v_heads / a.n_k_heads;
   const int kh = h / rep;
-  float* Sh = a.S + static_cast<size_t>(h) * kHD * kHD;
+  const bool swap = a.parity_dev && __ldcg(a.parity_dev);
+  float* S_rd = a.S;
+  float* S_wr = a.S_alt ? a.S_alt : a.S;
+  if (swap && a.S_alt) {
+    S_rd = a.S_alt;
+    S_wr = a.S;
+  }
+  const size_t hoff = static_cast<size_t>(h) * kHD * kHD;
   const int row0 = jr * R + warp * RPW;  // this warp's first state row
 
   // The state does not depend on the preceding kernel: load it before waiting.
   float S[RPW][4];
-  load_state<RPW>(S, Sh, row0, lane);
+  load_state<RPW>(S, S_rd + hoff, row0, lane);
   pdl_wait();
   pdl_trigger();
-  const bool swap = a.parity_dev && *a.parity_dev;
   const uint16_t* conv_in = swap ? a.conv_out : a.conv_in;
   uint16_t* conv_out = swap ? const_cast<uint16_t*>(a.conv_in) : a.conv_out;
 
@@ -300,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
     }
     __syncthreads();
   }
-  store_state<RPW>(S, Sh, row0, lane);
+  store_state<RPW>(S, S_wr + hoff, row0, lane);
   // new conv state = the last three inputs; q/k channels are shared by the
   // `rep` V-heads of a K-head, the first CTA of the first of them writes them
   if (col >= 0 && (region == 2 || (h % rep == 0 && jr == 0))) {
@@ -417,8 +423,10 @@ int launch_gdn(const GdnArgs& a, cudaStream_t st, bool pdl) {
   IAM_CHECK(a.n_k_heads > 0 && a.n_v_heads % a.n_k_heads == 0, "gdn: n_v_heads must be a multiple of n_k_heads");
   IAM_CHECK(a.rows > 0, "gdn: rows must be positive");
   IAM_CHECK(a.conv_in != a.conv_out, "gdn: conv state in/out must differ");
-  IAM_CHECK(a.ld_in % 4 == 0 && a.z_col % 4 == 0 && a.ld_out % 4 == 0 && aligned16(a.S) && aligned16(a.in),
+  IAM_CHECK(a.ld_in % 4 == 0 && a.z_col % 4 == 0 && a.ld_out % 4 == 0 && aligned16(a.S) && aligned16(a.in) &&
+                (!a.S_alt || aligned16(a.S_alt)),
             "gdn: 8-byte aligned rows required");
+  IAM_CHECK(a.S_alt != a.S, "gdn: the second state buffer must differ from the first");
   const int r = ensure_attrs();
   if (r != IAM_OK) return r;
   switch (gdn_split(a.n_v_heads, a.rows)) {

@@ -55,13 +55,17 @@ struct GdnArgs {
   const uint16_t* dt_bias;
   const uint16_t* norm_w;  // [dv]
   float* S;                // [n_v_heads, dv, dk]
+  float* S_alt;            // optional second state buffer: the state is read from S and written
+                           // here (the two swap when *parity_dev == 1); null = in place
   uint16_t* out;           // [rows, ld_out]
   int ld_out;
   int n_k_heads, n_v_heads;  // heads handled by this launch (shard-local)
   int key_dim, conv_dim;     // shard-local widths of the qkv block
   int rows;
   float eps;
-  const int* parity_dev;  // optional: when *parity_dev == 1, conv_in and conv_out swap roles
+  const int* parity_dev;  // optional: when *parity_dev == 1, conv_in/conv_out (and S/S_alt) swap roles;
+                          // read before the grid-dependency wait, so only a kernel launched without
+                          // programmatic overlap may have written it
 };
 int launch_gdn(const GdnArgs& a, cudaStream_t st, bool pdl);
 

@@ -63,6 +63,7 @@ _SIGS = {
     "iam_decode_step": (_i, [_vp, C.c_int32, _i, _vp]),
     "iam_generate": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp, _vp]),
     "iam_verify_device": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "iam_rollback": (_i, [_vp, _i, _vp]),
     "iam_read_tensor": (_i, [_vp, _cp, _vp, _sz]),
     "iam_read_hidden": (_i, [_vp, _vp, _i]),
     "iam_profile_step": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
@@ -294,6 +295,11 @@ class Engine:
         self._c(lib().iam_verify(self._h, t.ctypes.data_as(C.c_void_p), len(t), pos,
                                  out.ctypes.data_as(C.c_void_p), C.byref(acc)))
         return out, acc.value
+
+    def rollback(self, n_keep: int, stream=None):
+        """Keep the state after the first n_keep tokens of the last verify block
+        (accept_len + 1 after a greedy verify)."""
+        self._c(lib().iam_rollback(self._h, n_keep, _s(stream)))
 
     def generate(self, prompt, max_new: int, eos=(248046, 248044)):
         """Greedy generation from a reset state; returns the generated token ids."""
