@@ -286,6 +286,64 @@ def profile_step(args):
     e.close()
 
 
+def matmul_params(d) -> float:
+    """Weights of every 4-bit matmul of one step (the FLOPs of a token are twice this)."""
+    H, kd = d.hidden, d.gdn_k_heads * d.gdn_dk
+    gdn = H * (2 * kd + d.gdn_v_heads * d.gdn_dv) + H * d.gdn_v_heads * d.gdn_dv + 2 * H * d.gdn_v_heads \
+        + d.gdn_v_heads * d.gdn_dv * H
+    attn = H * 2 * d.n_heads * d.head_dim + 2 * H * d.n_kv_heads * d.head_dim + d.n_heads * d.head_dim * H
+    mlp = 3 * H * d.intermediate
+    n_attn = d.n_layers // d.full_attn_interval
+    return float((d.n_layers - n_attn) * gdn + n_attn * attn + d.n_layers * mlp + d.vocab * H)
+
+
+def sweep(args):
+    """Step time of the 64-layer verify against the verify width K (one engine,
+    one graph per K, device-resident tokens, context 1024): one JSON line per K
+    with the HBM fraction (step bytes / time) and the tensor fraction (2 x
+    matmul weights x K / time against the dense bf16 peak)."""
+    import numpy as np
+    import torch
+    import iam_b200 as I
+    ks = [int(v) for v in args.sweep.split(",")]
+    kmax = max(ks)
+    ksteps = args.warmup + args.steps
+    d = I.Dims.qwen35_27b(max_ctx=CTX + (ksteps + 2) * kmax + 64, max_rows=max(32, kmax))
+    e = I.Engine(d)
+    e.init_synthetic(SEED)
+    hbm, kind = peaks()
+    tc = 1643.5
+    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pp):
+        with open(pp) as f:
+            tc = float(json.load(f)["bf16_tflops"])
+    params = matmul_params(d)
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    rng = np.random.default_rng(SEED)
+    for K in ks:
+        e.state_init(SEED, CTX)
+        toks = torch.from_numpy(rng.integers(0, d.vocab, K).astype(np.int32)).cuda()
+        out = torch.zeros(K, dtype=torch.int32, device="cuda")
+        e.verify_device(toks.data_ptr(), K, CTX, out.data_ptr(), st.cuda_stream)
+        for _ in range(args.warmup - 1):
+            e.verify_device(toks.data_ptr(), K, -1, out.data_ptr(), st.cuda_stream)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for _ in range(args.steps):
+            e.verify_device(toks.data_ptr(), K, -1, out.data_ptr(), st.cuda_stream)
+        b.record(st)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        byts = e.step_bytes(K, CTX)
+        print(json.dumps({"sweep_k": K, "ms_per_step": round(ms, 4), "tokens_per_s": round(K * 1000.0 / ms, 1),
+                          "hbm_frac": round(byts / (ms / 1000.0) / 1e9 / hbm, 4),
+                          "tensor_frac": round(2.0 * params * K / (ms / 1000.0) / 1e12 / tc, 4),
+                          "peaks": {"hbm_gbs": hbm, "bf16_tflops": tc, "kind": kind}}), flush=True)
+    e.close()
+
+
 def profile_qmm(args):
     """A few launches of W4A16 matmul shapes "N,K,M[,mlx];..." (random codes)
     for ncu: through the tensor-core kernel on packed weights, or, with a
@@ -330,7 +388,10 @@ def main():
     ap.add_argument("--profile-step", action="store_true", help="two graph steps at --k, for ncu launch lists")
     ap.add_argument("--profile-qmm", default=None,
                     help="N,K,M[,mlx];...: a few launches of each matmul (tensor-core, or mma.sync on the MLX layout), for ncu")
+    ap.add_argument("--sweep", default=None, help="K1,K2,...: step time per verify width on one GPU")
     args = ap.parse_args()
+    if args.sweep:
+        return sweep(args)
     if args.profile_step:
         return profile_step(args)
     if args.profile_qmm:
