@@ -9,6 +9,7 @@ whole stack over the K tokens + lm_head argmax + accept length; positions
 advance by K every step (context 1024 -> 1024 + (W+S)*K).
 
   python bench.py [--gpus N] [--steps S] [--warmup W] [--k 32] [--impl reference]
+  python bench.py --batch 64 --k 8 [--ctx 4096]   # multi-sequence verify (one line, token-rows/s)
 
 With N > 1 (one process per GPU under torch.distributed.run) the step runs
 tensor-parallel over N GPUs (NCCL all-reduce of the row-parallel outputs), so
@@ -286,6 +287,106 @@ def profile_step(args):
     e.close()
 
 
+def run_batch(args, rank, world, local_rank):
+    """Multi-sequence verify: --batch sequences x --k draft tokens per step,
+    each sequence in its own slot (seeded GDN state, conv window, --ctx prior
+    KV tokens); value = token-rows verified per second (whole job; tensor
+    parallel over N GPUs, strong scaling)."""
+    import numpy as np
+    import torch
+    import iam_b200 as I
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    n, K, ctx = args.batch, args.k, args.ctx
+    steps = args.warmup + args.steps
+    dims = I.Dims.qwen35_27b(max_ctx=ctx + (2 * steps + 2) * K + 64, max_rows=n * K, max_seqs=n)
+    nccl_id = None
+    if world > 1:
+        obj = [I.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    eng = I.Engine(dims, device=local_rank, rank=rank, world=world, nccl_id=nccl_id)
+    eng.init_synthetic(SEED)
+    eng.state_init(SEED, ctx)
+    rng = np.random.default_rng(SEED)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    htoks = rng.integers(0, dims.vocab, (n, K)).astype(np.int32)
+    toks = torch.from_numpy(htoks.reshape(-1)).cuda()
+    pos0 = torch.full((n,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.zeros(n * K, dtype=torch.int32, device="cuda")
+    eng.verify_batch_device(toks.data_ptr(), n, K, pos0.data_ptr(), out.data_ptr(), None, sh)
+    for _ in range(args.warmup - 1):
+        eng.verify_batch_device(toks.data_ptr(), n, K, None, out.data_ptr(), None, sh)
+    barrier()
+    clk = ClockSampler(local_rank)
+    clk.start()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        eng.verify_batch_device(toks.data_ptr(), n, K, None, out.data_ptr(), None, sh)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    clocks = clk.stop()
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    barrier()
+    # end to end through the public C API: host tokens and positions in, argmax and accept lengths out
+    pos = np.full(n, ctx + steps * K, np.int32)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.verify_batch(htoks, pos)
+        pos += K
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if dist is not None:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    byts = eng.step_bytes_batch(n, K, ctx)
+    params = matmul_params(dims)
+    eng.close()
+    if rank != 0:
+        return
+    hbm, kind = peaks()
+    tc = 1643.5
+    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pp):
+        with open(pp) as f:
+            tc = float(json.load(f)["bf16_tflops"])
+    rows = n * K
+    gbs = byts / (ms / 1000.0) / 1e9
+    tfs = 2.0 * params * rows / world / (ms / 1000.0) / 1e12
+    line = {
+        "metric": f"verified token-rows/sec, {n} sequences x K={K}, ctx {ctx}",
+        "value": rows * 1000.0 / ms, "unit": "token-rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"qwen3.5-27b-shape 64-layer 4-bit multi-sequence verify, {n} x K={K}, ctx {ctx}",
+                   "sequences": n, "K": K, "ctx": ctx, "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2 (14.4 GB of weights, 19 GB of GDN state per step)"},
+        "roofline": {"hbm": {"bytes_per_step_per_gpu": byts, "achieved_gbs": gbs, "peak_gbs": hbm,
+                             "frac": gbs / hbm, "peak_kind": kind},
+                     "tensor": {"achieved_tflops_per_gpu": tfs, "peak_tflops": tc, "frac": tfs / tc}},
+        "e2e": {"value": rows / e2e_s, "unit": "token-rows/s", "h2d_bytes_per_step": 4 * (n + rows),
+                "d2h_bytes_per_step": 4 * (n + rows)},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def matmul_params(d) -> float:
     """Weights of every 4-bit matmul of one step (the FLOPs of a token are twice this)."""
     H, kd = d.hidden, d.gdn_k_heads * d.gdn_dk
@@ -389,6 +490,8 @@ def main():
     ap.add_argument("--profile-qmm", default=None,
                     help="N,K,M[,mlx];...: a few launches of each matmul (tensor-core, or mma.sync on the MLX layout), for ncu")
     ap.add_argument("--sweep", default=None, help="K1,K2,...: step time per verify width on one GPU")
+    ap.add_argument("--batch", type=int, default=0, help="sequences of a multi-sequence verify step (with --k)")
+    ap.add_argument("--ctx", type=int, default=4096, help="prior KV tokens per sequence of --batch")
     args = ap.parse_args()
     if args.sweep:
         return sweep(args)
@@ -411,6 +514,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.batch:
+            run_batch(args, rank, world, local_rank)
         else:
             run_gpu(args, rank, world, local_rank)
     finally:

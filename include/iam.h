@@ -207,7 +207,8 @@ typedef struct iam_dims {
   int group_size;        /* 64 */
   float eps;             /* 1e-6 */
   int max_ctx;           /* KV-cache capacity in tokens */
-  int max_rows;          /* largest verify width (tokens per step) */
+  int max_rows;          /* largest verify width (tokens per step, all sequences) */
+  int max_seqs;          /* sequence slots for iam_verify_batch (1: one sequence) */
 } iam_dims;
 
 /* Qwen3.5-27B defaults (full_forward.swift:18-49). */
@@ -278,8 +279,8 @@ int iam_check_safetensors(const iam_dims* dims, const char* const* paths, int n_
 int iam_init_synthetic(iam_engine* e, uint64_t seed);
 
 /* Seeded recurrent state: conv state N(0,1), S N(0,0.01) and `ctx` prior KV
- * tokens N(0,1); or zero state (the reference's resetAllState) when seed == 0
- * and ctx == 0. */
+ * tokens N(0,1) in every sequence slot (each slot its own streams); or zero
+ * state (the reference's resetAllState) when seed == 0 and ctx == 0. */
 int iam_state_init(iam_engine* e, uint64_t seed, int ctx);
 int iam_state_reset(iam_engine* e);
 
@@ -321,11 +322,33 @@ int iam_rollback(iam_engine* e, int n_keep, void* stream);
 int iam_generate(iam_engine* e, const int32_t* prompt, int n_prompt, int max_new, const int32_t* eos, int n_eos,
                  int32_t* out, int* n_out);
 
+/* Multi-sequence batch verify: n_seq independent sequences (slots
+ * 0..n_seq-1, each with its own GDN state, conv window and KV cache) verify K
+ * tokens each in one step; the weights are streamed once for all n_seq * K
+ * rows.  tokens int32 [n_seq][K] (row 0 of each is the token being decoded),
+ * pos int32 [n_seq] (each sequence's position), argmax_out int32 [n_seq][K],
+ * accept_len int32 [n_seq] (per sequence, as iam_verify).  Slots from n_seq
+ * on are untouched.  Requires n_seq <= max_seqs, n_seq * K <= max_rows and
+ * pos[s] + K <= max_ctx.  iam_rollback applies to single-sequence verifies
+ * only.  Follows batch_verify_27b.swift:141-274 (the M-row loop) with the M
+ * rows split into sequences; the reference has no multi-sequence state. */
+int iam_verify_batch(iam_engine* e, const int32_t* tokens, int n_seq, int K, const int32_t* pos,
+                     int32_t* argmax_out, int32_t* accept_len);
+/* Device-resident variant (benchmarking): d_tokens int32 [n_seq * K]; d_pos
+ * int32 [n_seq] or NULL to continue from the positions the previous batch
+ * step left; d_argmax int32 [n_seq * K] and d_accept int32 [n_seq] may be
+ * NULL.  Nothing is synchronised. */
+int iam_verify_batch_device(iam_engine* e, const int32_t* d_tokens, int n_seq, int K, const int32_t* d_pos,
+                            int32_t* d_argmax, int32_t* d_accept, void* stream);
+
 /* Device-resident variant for benchmarking: tokens/outputs stay on the GPU
  * (d_tokens int32 [K], d_argmax int32 [K]) and nothing is synchronised. */
 int iam_verify_device(iam_engine* e, const int32_t* d_tokens, int K, int pos, int32_t* d_argmax, void* stream);
 
-/* Read back device copies of internal tensors for tests (host buffers). */
+/* Read back device copies of internal tensors for tests (host buffers).
+ * State tensors ("state.S.<layer>", "state.conv.<layer>",
+ * "state.k_cache.<layer>", "state.v_cache.<layer>") hold every sequence
+ * slot, slot after slot. */
 int iam_read_tensor(iam_engine* e, const char* name, void* host_ptr, size_t bytes);
 /* Final normed hidden [K, hidden] of the last step (bf16). */
 int iam_read_hidden(iam_engine* e, uint16_t* host_ptr, int K);
@@ -340,6 +363,9 @@ int iam_step_launches(iam_engine* e, int K);
 /* Algorithmic HBM bytes of one step of width K at position pos (weights +
  * state read/write + KV read), per GPU. */
 double iam_step_bytes(iam_engine* e, int K, int pos);
+/* The same for a multi-sequence step: weights once, per-sequence bytes
+ * n_seq times (every sequence at position pos). */
+double iam_step_bytes_batch(iam_engine* e, int n_seq, int K, int pos);
 
 #ifdef __cplusplus
 }

@@ -22,7 +22,8 @@ constexpr int kHeadDim = 256;
 constexpr int kChunkTok = 32;
 constexpr int kKvStride = kHeadDim + 8;  // padded smem row (bf16 elements)
 
-__device__ __forceinline__ int cur_pos(const AttnArgs& a) { return a.pos_dev ? *a.pos_dev : a.pos; }
+// Position of row 0 of sequence sq (one sequence: sq = 0).
+__device__ __forceinline__ int cur_pos(const AttnArgs& a, int sq = 0) { return a.pos_dev ? a.pos_dev[sq] : a.pos; }
 
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   f[0] = lo_bf(v.x); f[1] = hi_bf(v.x); f[2] = lo_bf(v.y); f[3] = hi_bf(v.y);
@@ -33,6 +34,9 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 }
 
 // ---------------------------------------------------------------- prep
+// kSeq: rows of several sequences (AttnArgs n_seq); row t belongs to sequence
+// t / seq_rows, whose own position and caches it uses.
+template <bool kSeq>
 __global__ void __launch_bounds__(256) attn_prep_kernel(const AttnArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -42,7 +46,12 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const AttnArgs a) {
   if (head >= a.n_heads + a.n_kv_heads) return;
   const bool is_q = head < a.n_heads;
   const int kvh = head - a.n_heads;
-  const int pos = cur_pos(a) + t;
+  int sq = 0, tt = t;
+  if constexpr (kSeq) {
+    sq = t / a.seq_rows;
+    tt = t - sq * a.seq_rows;
+  }
+  const int pos = cur_pos(a, sq) + tt;
   if (pos < 0 || pos >= a.max_ctx) return;  // the host keeps pos + rows <= max_ctx
   const uint16_t* row = a.qkv + static_cast<size_t>(t) * a.ld_qkv;
   const uint16_t* src = is_q ? row + static_cast<size_t>(head) * 2 * kHeadDim : row + a.k_col + kvh * kHeadDim;
@@ -72,7 +81,8 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const AttnArgs a) {
   if (is_q) {
     *reinterpret_cast<uint4*>(a.q_buf + (static_cast<size_t>(t) * a.n_heads + head) * kHeadDim + 8 * lane) = pack8(x);
   } else {
-    const size_t off = (static_cast<size_t>(pos) * a.n_kv_heads + kvh) * kHeadDim + 8 * lane;
+    size_t off = (static_cast<size_t>(pos) * a.n_kv_heads + kvh) * kHeadDim + 8 * lane;
+    if constexpr (kSeq) off += static_cast<size_t>(sq) * a.seq_kv;
     *reinterpret_cast<uint4*>(a.k_cache + off) = pack8(x);
     *reinterpret_cast<uint4*>(a.v_cache + off) =
         *reinterpret_cast<const uint4*>(row + a.v_col + kvh * kHeadDim + 8 * lane);
@@ -92,17 +102,31 @@ struct DecodeSmem {
   uint16_t q[kRowBlock * 8][kHeadDim];
 };
 
+// kSeq: grid.z = sequence x row block of the sequence (AttnArgs n_seq).
+template <bool kSeq>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
   pdl_wait();
   pdl_trigger();
-  const int split = blockIdx.x, kvh = blockIdx.y, t0 = blockIdx.z * kRowBlock;
+  int sq = 0, zb = blockIdx.z, srows = a.rows, rbase = 0;
+  const uint16_t* kc = a.k_cache;
+  const uint16_t* vc = a.v_cache;
+  if constexpr (kSeq) {
+    const int bps = (a.seq_rows + kRowBlock - 1) / kRowBlock;
+    sq = blockIdx.z / bps;
+    zb = blockIdx.z - sq * bps;
+    srows = a.seq_rows;
+    rbase = sq * a.seq_rows;
+    kc += static_cast<size_t>(sq) * a.seq_kv;
+    vc += static_cast<size_t>(sq) * a.seq_kv;
+  }
+  const int split = blockIdx.x, kvh = blockIdx.y, t0 = zb * kRowBlock;  // t0: row within the sequence
   const int rep = a.n_heads / a.n_kv_heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nrows = min(kRowBlock, a.rows - t0);
+  const int nrows = min(kRowBlock, srows - t0);
   const int npairs = nrows * rep;
-  const int pos0 = cur_pos(a);
+  const int pos0 = cur_pos(a, sq);
   // the block's longest context decides its chunk range; shorter rows mask
   const int last_max = min(pos0 + t0 + nrows - 1, a.max_ctx - 1);
   const int nch = last_max / kChunkTok + 1;
@@ -110,7 +134,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
   const int c_end = static_cast<int>((static_cast<long long>(split + 1) * nch) / a.nsplit);
   for (int i = threadIdx.x; i < npairs * (kHeadDim / 8); i += blockDim.x) {
     const int pr = i / (kHeadDim / 8), d8 = (i % (kHeadDim / 8)) * 8;
-    const int t = t0 + pr / rep, h = kvh * rep + pr % rep;
+    const int t = rbase + t0 + pr / rep, h = kvh * rep + pr % rep;
     *reinterpret_cast<uint4*>(&sm.q[pr][d8]) =
         *reinterpret_cast<const uint4*>(a.q_buf + (static_cast<size_t>(t) * a.n_heads + h) * kHeadDim + d8);
   }
@@ -131,8 +155,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
       uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
       if (r < nstage) {
         const size_t off = (static_cast<size_t>(p0 + r) * a.n_kv_heads + kvh) * kHeadDim + d8;
-        kk = *reinterpret_cast<const uint4*>(a.k_cache + off);
-        vv = *reinterpret_cast<const uint4*>(a.v_cache + off);
+        kk = *reinterpret_cast<const uint4*>(kc + off);
+        vv = *reinterpret_cast<const uint4*>(vc + off);
       }
       *reinterpret_cast<uint4*>(&sm.k[r][d8]) = kk;
       *reinterpret_cast<uint4*>(&sm.v[r][d8]) = vv;
@@ -179,7 +203,7 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnArgs a) {
   for (int pp = 0; pp < kMaxPairs; ++pp) {
     const int pr = warp + 8 * pp;
     if (pr < npairs) {
-      const int t = t0 + pr / rep, h = kvh * rep + pr % rep;
+      const int t = rbase + t0 + pr / rep, h = kvh * rep + pr % rep;
       const size_t part = (static_cast<size_t>(t) * a.n_heads + h) * a.nsplit + split;
       float4* po = reinterpret_cast<float4*>(a.part_o + part * kHeadDim + 8 * lane);
       po[0] = make_float4(o[pp][0], o[pp][1], o[pp][2], o[pp][3]);
@@ -224,6 +248,8 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// kSeq: grid.z = sequence x 64-pair tile of the sequence (AttnArgs n_seq).
+template <bool kSeq>
 __global__ void __launch_bounds__(128, 1) attn_decode_tc_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint16_t* sq = reinterpret_cast<uint16_t*>(smem_raw);
@@ -231,11 +257,23 @@ __global__ void __launch_bounds__(128, 1) attn_decode_tc_kernel(const AttnArgs a
   uint16_t* sv = sk + kTcKeys * kTcStride;
   pdl_wait();
   pdl_trigger();
-  const int split = blockIdx.x, kvh = blockIdx.y, p0 = blockIdx.z * kTcPairs;
   const int rep = a.n_heads / a.n_kv_heads;
-  const int npairs = a.rows * rep;
+  int seq = 0, zb = blockIdx.z, srows = a.rows, rbase = 0;
+  const uint16_t* kc = a.k_cache;
+  const uint16_t* vc = a.v_cache;
+  if constexpr (kSeq) {
+    const int tps = (a.seq_rows * rep + kTcPairs - 1) / kTcPairs;
+    seq = blockIdx.z / tps;
+    zb = blockIdx.z - seq * tps;
+    srows = a.seq_rows;
+    rbase = seq * a.seq_rows;
+    kc += static_cast<size_t>(seq) * a.seq_kv;
+    vc += static_cast<size_t>(seq) * a.seq_kv;
+  }
+  const int split = blockIdx.x, kvh = blockIdx.y, p0 = zb * kTcPairs;  // pairs within the sequence
+  const int npairs = srows * rep;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
-  const int pos0 = cur_pos(a);
+  const int pos0 = cur_pos(a, seq);
   const int t_hi = (min(p0 + kTcPairs, npairs) - 1) / rep;
   const int nkeys = min(pos0 + t_hi, a.max_ctx - 1) + 1;
   const int nch = (nkeys + kTcKeys - 1) / kTcKeys;
@@ -247,7 +285,7 @@ __global__ void __launch_bounds__(128, 1) attn_decode_tc_kernel(const AttnArgs a
   const int qpos_lo = pl < npairs ? min(pos0 + pl / rep, a.max_ctx - 1) : -1;
   const int qpos_hi = ph < npairs ? min(pos0 + ph / rep, a.max_ctx - 1) : -1;
   auto part_of = [&](int p) {
-    const int t = p / rep, h = kvh * rep + p % rep;
+    const int t = rbase + p / rep, h = kvh * rep + p % rep;
     return (static_cast<size_t>(t) * a.n_heads + h) * a.nsplit + split;
   };
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
@@ -263,7 +301,7 @@ __global__ void __launch_bounds__(128, 1) attn_decode_tc_kernel(const AttnArgs a
       const int p = p0 + r;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (p < npairs) {
-        const int t = p / rep, h = kvh * rep + p % rep;
+        const int t = rbase + p / rep, h = kvh * rep + p % rep;
         v = *reinterpret_cast<const uint4*>(a.q_buf + (static_cast<size_t>(t) * a.n_heads + h) * kHeadDim + d8);
       }
       *reinterpret_cast<uint4*>(sq + r * kTcStride + d8) = v;
@@ -278,8 +316,8 @@ __global__ void __launch_bounds__(128, 1) attn_decode_tc_kernel(const AttnArgs a
         uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
         if (kbase + r < nkeys) {
           const size_t off = (static_cast<size_t>(kbase + r) * a.n_kv_heads + kvh) * kHeadDim + d8;
-          kk = *reinterpret_cast<const uint4*>(a.k_cache + off);
-          vv = *reinterpret_cast<const uint4*>(a.v_cache + off);
+          kk = *reinterpret_cast<const uint4*>(kc + off);
+          vv = *reinterpret_cast<const uint4*>(vc + off);
         }
         *reinterpret_cast<uint4*>(sk + r * kTcStride + d8) = kk;
         *reinterpret_cast<uint4*>(sv + r * kTcStride + d8) = vv;
@@ -465,14 +503,20 @@ OpScratch g_scratch[64];
 int launch_attn_prep(const AttnArgs& a, cudaStream_t st, bool pdl) {
   IAM_CHECK(a.head_dim == kHeadDim, "attention: head_dim 256 required");
   IAM_CHECK(a.rotary_dim % 8 == 0 && a.rotary_dim <= kHeadDim, "attention: rotary_dim % 8 == 0 required");
-  return launch_k(attn_prep_kernel, dim3(a.rows, (a.n_heads + a.n_kv_heads + 7) / 8), dim3(256), 0, st, pdl, a);
+  const dim3 grid(a.rows, (a.n_heads + a.n_kv_heads + 7) / 8);
+  if (a.n_seq > 1) {
+    IAM_CHECK(a.seq_rows >= 1 && a.rows == a.n_seq * a.seq_rows && a.pos_dev, "attention: sequence rows / positions");
+    return launch_k(attn_prep_kernel<true>, grid, dim3(256), 0, st, pdl, a);
+  }
+  return launch_k(attn_prep_kernel<false>, grid, dim3(256), 0, st, pdl, a);
 }
 
 int attn_init_attrs() {
   if (!g_attn_attr) {
-    IAM_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(DecodeSmem)));
-    IAM_CUDA(cudaFuncSetAttribute(attn_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(kTcSmem)));
+    for (auto* k : {attn_decode_kernel<false>, attn_decode_kernel<true>})
+      IAM_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(DecodeSmem)));
+    for (auto* k : {attn_decode_tc_kernel<false>, attn_decode_tc_kernel<true>})
+      IAM_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTcSmem)));
     g_attn_attr = true;
   }
   return IAM_OK;
@@ -487,12 +531,24 @@ int launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int r = attn_init_attrs();
   if (r != IAM_OK) return r;
   IAM_CHECK(a.nsplit >= 1 && a.nsplit <= 64, "attention: 1..64 context splits");
-  const int npairs = a.rows * (a.n_heads / a.n_kv_heads);
+  const int rep = a.n_heads / a.n_kv_heads;
+  if (a.n_seq > 1) {  // pairs of one sequence per CTA
+    IAM_CHECK(a.seq_rows >= 1 && a.rows == a.n_seq * a.seq_rows && a.pos_dev, "attention: sequence rows / positions");
+    const int sp = a.seq_rows * rep;
+    if (sp >= kTcMinPairs)
+      return launch_k(attn_decode_tc_kernel<true>,
+                      dim3(a.nsplit, a.n_kv_heads, a.n_seq * ((sp + kTcPairs - 1) / kTcPairs)), dim3(128), kTcSmem,
+                      st, pdl, a);
+    return launch_k(attn_decode_kernel<true>,
+                    dim3(a.nsplit, a.n_kv_heads, a.n_seq * ((a.seq_rows + kRowBlock - 1) / kRowBlock)), dim3(256),
+                    sizeof(DecodeSmem), st, pdl, a);
+  }
+  const int npairs = a.rows * rep;
   if (npairs >= kTcMinPairs)
-    return launch_k(attn_decode_tc_kernel, dim3(a.nsplit, a.n_kv_heads, (npairs + kTcPairs - 1) / kTcPairs),
+    return launch_k(attn_decode_tc_kernel<false>, dim3(a.nsplit, a.n_kv_heads, (npairs + kTcPairs - 1) / kTcPairs),
                     dim3(128), kTcSmem, st, pdl, a);
-  return launch_k(attn_decode_kernel, dim3(a.nsplit, a.n_kv_heads, (a.rows + kRowBlock - 1) / kRowBlock), dim3(256),
-                  sizeof(DecodeSmem), st, pdl, a);
+  return launch_k(attn_decode_kernel<false>, dim3(a.nsplit, a.n_kv_heads, (a.rows + kRowBlock - 1) / kRowBlock),
+                  dim3(256), sizeof(DecodeSmem), st, pdl, a);
 }
 
 int launch_attn_combine(const AttnArgs& a, cudaStream_t st, bool pdl) {

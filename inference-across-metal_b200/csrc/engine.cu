@@ -133,16 +133,20 @@ struct EngineImpl {
   uint16_t* final_norm = nullptr;
   QW lm;
 
-  // state; S holds two copies of every GDN layer's state (s_half floats
-  // apart) and conv two windows, swapped each step by *d_parity: a step reads
-  // the state before it and leaves that copy intact, which is what
-  // iam_rollback replays the accepted rows from
+  // state, per layer one block of max_seqs sequence slots (slot 0: the
+  // single-sequence entry points); S holds two copies of every slot's state
+  // (s_half floats apart) and conv two windows, swapped each step by the
+  // slot's parity word d_parity[slot]: a step reads the state before it and
+  // leaves that copy intact, which is what iam_rollback replays the accepted
+  // rows from
+  int max_seqs = 1;
+  size_t s_per = 0;  // floats of one slot's state in one layer
   float* S = nullptr;
   size_t s_half = 0;
   uint16_t* conv[2] = {nullptr, nullptr};
   uint16_t* kc = nullptr;
   uint16_t* vc = nullptr;
-  int* d_parity = nullptr;
+  int* d_parity = nullptr;  // [max_seqs]
   int parity = 0;
   int last_K = 0;  // rows of the last verify block since the state was set (0: none to roll back)
 
@@ -165,8 +169,19 @@ struct EngineImpl {
   StepIn* h_in = nullptr;
   int32_t* h_out = nullptr;
 
+  // multi-sequence steps: positions [max_seqs] then tokens [max_rows] (d_bin,
+  // pinned mirror h_bin); accept lengths [max_seqs] then argmax [max_rows]
+  // (d_bout, h_bout)
+  int32_t* d_bin = nullptr;
+  int32_t* h_bin = nullptr;
+  int32_t* d_bout = nullptr;
+  int32_t* h_bout = nullptr;
+
   std::map<int, cudaGraphExec_t> graphs;
-  int cur_rows = 0;  // verify width of the step being enqueued
+  std::map<std::pair<int, int>, cudaGraphExec_t> bgraphs;  // by (n_seq, K)
+  int cur_rows = 0;  // rows of the step being enqueued (all sequences)
+  int cur_seqs = 0;  // sequences of a multi-sequence step being enqueued (0: the single-sequence step)
+  int cur_k = 0;     // rows per sequence of that step
   int host_pos = 0;  // the position the next device-driven step starts at
   bool pdl = true;
   std::vector<ProfEntry>* prof = nullptr;
@@ -406,16 +421,18 @@ int alloc_all(EngineImpl& e) {
   }
 
   // state
-  const size_t s_per = static_cast<size_t>(e.gv_l) * d.gdn_dk * d.gdn_dv;
-  e.s_half = static_cast<size_t>(e.n_gdn) * s_per;
+  e.max_seqs = d.max_seqs;
+  const size_t slots = static_cast<size_t>(e.max_seqs);
+  e.s_per = static_cast<size_t>(e.gv_l) * d.gdn_dk * d.gdn_dv;
+  e.s_half = static_cast<size_t>(e.n_gdn) * slots * e.s_per;
   E_CUDA(cudaMalloc(&e.S, std::max<size_t>(1, 2 * e.s_half) * sizeof(float)));
   for (int i = 0; i < 2; ++i)
-    E_CUDA(cudaMalloc(&e.conv[i], std::max<size_t>(1, static_cast<size_t>(e.n_gdn) * 3 * e.conv_l) * 2));
-  const size_t kv = static_cast<size_t>(e.n_attn) * d.max_ctx * e.hkv_l * d.head_dim;
+    E_CUDA(cudaMalloc(&e.conv[i], std::max<size_t>(1, static_cast<size_t>(e.n_gdn) * slots * 3 * e.conv_l) * 2));
+  const size_t kv = static_cast<size_t>(e.n_attn) * slots * d.max_ctx * e.hkv_l * d.head_dim;
   E_CUDA(cudaMalloc(&e.kc, std::max<size_t>(1, kv) * 2));
   E_CUDA(cudaMalloc(&e.vc, std::max<size_t>(1, kv) * 2));
-  E_CUDA(cudaMalloc(&e.d_parity, sizeof(int)));
-  E_CUDA(cudaMemset(e.d_parity, 0, sizeof(int)));
+  E_CUDA(cudaMalloc(&e.d_parity, slots * sizeof(int)));
+  E_CUDA(cudaMemset(e.d_parity, 0, slots * sizeof(int)));
 
   // activations
   const int R = d.max_rows;
@@ -456,6 +473,11 @@ int alloc_all(EngineImpl& e) {
   E_CUDA(cudaMemset(e.d_err, 0, sizeof(int)));
   E_CUDA(cudaMallocHost(&e.h_in, sizeof(int32_t) * (1 + R)));
   E_CUDA(cudaMallocHost(&e.h_out, sizeof(int32_t) * (1 + R)));
+  E_CUDA(cudaMalloc(&e.d_bin, sizeof(int32_t) * (slots + R)));
+  E_CUDA(cudaMemset(e.d_bin, 0, sizeof(int32_t) * (slots + R)));
+  E_CUDA(cudaMalloc(&e.d_bout, sizeof(int32_t) * (slots + R)));
+  E_CUDA(cudaMallocHost(&e.h_bin, sizeof(int32_t) * (slots + R)));
+  E_CUDA(cudaMallocHost(&e.h_bout, sizeof(int32_t) * (slots + R)));
 
   // RoPE table [max_ctx][rotary/2] (cos, sin): precomputeRoPE in double
   // (full_forward.swift:734-743)
@@ -546,10 +568,12 @@ int run_qmm(EngineImpl& e, QmmArgs& a, const char* kind, double bytes) {
 // GPU; fp32 partials + NCCL all-reduce + residual kernel across GPUs.
 int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, const uint16_t* resid, uint16_t* out);
 
-// The GDN kernel's arguments for layer L over the first `rows` rows of the
-// layer's projections of the current block (e.gin); the state buffers and
-// conv windows are picked on the device by *d_parity.
-GdnArgs gdn_args(EngineImpl& e, const Layer& L, int rows) {
+// The GDN kernel's arguments for layer L over the first `rows` rows of each
+// of n_seq sequences (slots 0..n_seq-1; sequence q's rows follow the q * rows
+// before them) of the layer's projections of the current block (e.gin); the
+// state buffers and conv windows of each slot are picked on the device by its
+// parity word.
+GdnArgs gdn_args(EngineImpl& e, const Layer& L, int rows, int n_seq) {
   const iam_dims& d = e.d;
   GdnArgs g = {};
   g.in = e.gin + static_cast<size_t>(L.idx) * d.max_rows * e.ld_in;
@@ -558,15 +582,18 @@ GdnArgs gdn_args(EngineImpl& e, const Layer& L, int rows) {
   g.b_col = e.conv_l + e.vd_l;
   g.a_col = e.conv_l + e.vd_l + e.gv_l;
   g.conv_w = L.conv_w;
-  const size_t coff = static_cast<size_t>(L.idx) * 3 * e.conv_l;
+  const size_t coff = static_cast<size_t>(L.idx) * e.max_seqs * 3 * e.conv_l;
   g.conv_in = e.conv[0] + coff;
   g.conv_out = e.conv[1] + coff;
   g.parity_dev = e.d_parity;
   g.A_log = L.A_log;
   g.dt_bias = L.dt_bias;
   g.norm_w = L.norm_w;
-  g.S = e.S + static_cast<size_t>(L.idx) * e.gv_l * d.gdn_dk * d.gdn_dv;
+  g.S = e.S + static_cast<size_t>(L.idx) * e.max_seqs * e.s_per;
   g.S_alt = g.S + e.s_half;
+  g.n_seq = n_seq;
+  g.seq_S = e.s_per;
+  g.seq_conv = static_cast<size_t>(3) * e.conv_l;
   g.out = e.mid;
   g.ld_out = e.vd_l;
   g.n_k_heads = e.gk_l;
@@ -603,7 +630,7 @@ int enqueue_gdn(EngineImpl& e, const Layer& L, int K) {
   for (int i = 0; i < 4; ++i) a.seg[i].ldo = e.ld_in;
   E_RUN(run_qmm(e, a, "qmm", qbytes(L.qkv) + qbytes(L.z) + qbytes(L.bproj) + qbytes(L.aproj)));
 
-  const GdnArgs g = gdn_args(e, L, K);
+  const GdnArgs g = gdn_args(e, L, e.cur_seqs ? e.cur_k : K, std::max(1, e.cur_seqs));
   {
     Recorder rec(e, "gdn", 2.0 * e.gv_l * d.gdn_dk * d.gdn_dv * 4 + 2.0 * 3 * e.conv_l * 2);
     E_RUN(launch_gdn(g, e.stream, e.pdl));
@@ -641,7 +668,8 @@ int enqueue_attn(EngineImpl& e, const Layer& L, int K) {
   t.v_col = 2 * e.hq_l * hd + e.hkv_l * hd;
   t.q_norm_w = L.q_norm;
   t.k_norm_w = L.k_norm;
-  const size_t kvoff = static_cast<size_t>(L.idx) * d.max_ctx * e.hkv_l * hd;
+  const size_t seq_kv = static_cast<size_t>(d.max_ctx) * e.hkv_l * hd;
+  const size_t kvoff = static_cast<size_t>(L.idx) * e.max_seqs * seq_kv;
   t.k_cache = e.kc + kvoff;
   t.v_cache = e.vc + kvoff;
   t.q_buf = e.q_buf;
@@ -657,6 +685,12 @@ int enqueue_attn(EngineImpl& e, const Layer& L, int K) {
   t.max_ctx = d.max_ctx;
   t.rows = K;
   t.pos_dev = &e.d_in->pos;
+  if (e.cur_seqs) {
+    t.n_seq = e.cur_seqs;
+    t.seq_rows = e.cur_k;
+    t.seq_kv = seq_kv;
+    t.pos_dev = e.d_bin;
+  }
   t.chunk = attn_chunk_tokens();
   t.nsplit = kNSplit;
   t.eps = d.eps;
@@ -730,7 +764,7 @@ int enqueue_rollback(EngineImpl& e, int K, int n_keep, cudaStream_t st) {
   rewind_kernel<<<1, 1, 0, st>>>(e.d_in, e.d_parity, K);
   E_CUDA(cudaGetLastError());
   for (const Layer& L : e.layers)
-    if (!L.attn) E_RUN(launch_gdn(gdn_args(e, L, n_keep), st, false));
+    if (!L.attn) E_RUN(launch_gdn(gdn_args(e, L, n_keep, 1), st, false));
   advance_kernel<<<1, 1, 0, st>>>(e.d_in, e.d_parity, n_keep);
   E_CUDA(cudaGetLastError());
   return IAM_OK;
@@ -767,12 +801,56 @@ int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, c
                   resid, out, n);
 }
 
-int enqueue_step(EngineImpl& e, int K) {
+__global__ void advance_seqs_kernel(int32_t* pos, int* parity, int n_seq, int K) {
+  for (int q = threadIdx.x; q < n_seq; q += blockDim.x) {
+    pos[q] += K;
+    parity[q] ^= 1;
+  }
+}
+
+// The multi-sequence step's end: per-row argmax (lm_head keys reduced one CTA
+// a row, across ranks through an all-gather of the rows' best keys), each
+// sequence's accept length, and the slots' positions and parities advanced.
+int enqueue_finish_seqs(EngineImpl& e, int nparts, int n_seq, int Kseq) {
+  const int rows = n_seq * Kseq;
+  const int32_t* tokens = e.d_bin + e.max_seqs;
+  int32_t* argmax = e.d_bout + e.max_seqs;
+  if (e.world == 1) {
+    Recorder rec(e, "finalize", 8.0 * nparts * rows);
+    E_RUN(launch_finalize_batch(e.keys, nparts, e.d.max_rows, n_seq, Kseq, tokens, argmax, e.d_bout, e.stream,
+                                e.pdl));
+  } else {
+    unsigned long long* mine = e.best + static_cast<size_t>(e.rank) * rows;
+    {
+      Recorder rec(e, "finalize", 8.0 * nparts * rows);
+      E_RUN(launch_best_rows(e.keys, nparts, e.d.max_rows, rows, mine, e.stream, e.pdl));
+    }
+    {
+      Recorder rec(e, "allgather", 8.0 * e.world * rows);
+      E_RUN(nccl_allgather_u64(e.comm, mine, e.best, static_cast<size_t>(rows), e.stream));
+    }
+    Recorder rec(e, "finalize", 8.0 * e.world * rows);
+    E_RUN(launch_finalize_batch(e.best, e.world, rows, n_seq, Kseq, tokens, argmax, e.d_bout, e.stream, false));
+  }
+  Recorder rec(e, "advance", 8.0 * n_seq);
+  advance_seqs_kernel<<<1, 256, 0, e.stream>>>(e.d_bin, e.d_parity, n_seq, Kseq);
+  E_CUDA(cudaGetLastError());
+  return IAM_OK;
+}
+
+// One step of the whole model: K rows of the single sequence (n_seq = 0), or
+// K rows of each of the sequences in slots 0..n_seq-1 (n_seq >= 1, the
+// multi-sequence step: inputs and outputs in d_bin / d_bout).
+int enqueue_step(EngineImpl& e, int n_seq, int Kseq) {
   const iam_dims& d = e.d;
+  const int K = n_seq ? n_seq * Kseq : Kseq;  // rows of the step
   e.cur_rows = K;
+  e.cur_seqs = n_seq;
+  e.cur_k = Kseq;
+  const int32_t* tokens = n_seq ? e.d_bin + e.max_seqs : e.d_in->tokens;
   {
     Recorder rec(e, "embed", 4.0 * K * d.hidden);
-    E_RUN(launch_embed_bf16(e.embed, e.d_in->tokens, e.hidden, K, d.hidden, d.vocab, e.d_err, e.stream, false));
+    E_RUN(launch_embed_bf16(e.embed, tokens, e.hidden, K, d.hidden, d.vocab, e.d_err, e.stream, false));
   }
   for (const Layer& L : e.layers) {
     if (L.attn) E_RUN(enqueue_attn(e, L, K));
@@ -796,6 +874,7 @@ int enqueue_step(EngineImpl& e, int K) {
   E_RUN(run_qmm(e, a, "qmm", qbytes(e.lm)));
   // one key row per 128-row lm_head tile
   const int nparts = qp_tiles(e.lm.rows, false);
+  if (n_seq) return enqueue_finish_seqs(e, nparts, n_seq, Kseq);
   if (e.world == 1) {
     Recorder rec(e, "finalize", 8.0 * nparts * K);
     E_RUN(launch_finalize(e.keys, nparts, d.max_rows, K, e.d_in->tokens, e.d_out + 1, e.d_out, e.stream, e.pdl));
@@ -828,7 +907,7 @@ int get_graph(EngineImpl& e, int K, cudaGraphExec_t* out) {
   }
   cudaGraph_t g = nullptr;
   E_CUDA(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
-  const int r = enqueue_step(e, K);
+  const int r = enqueue_step(e, 0, K);
   cudaGraph_t gg = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(e.stream, &gg);
   if (r != IAM_OK) {
@@ -842,6 +921,31 @@ int get_graph(EngineImpl& e, int K, cudaGraphExec_t* out) {
   cudaGraphDestroy(g);
   E_CUDA(ie);
   e.graphs[K] = ex;
+  *out = ex;
+  return IAM_OK;
+}
+
+int get_batch_graph(EngineImpl& e, int n_seq, int K, cudaGraphExec_t* out) {
+  const auto key = std::make_pair(n_seq, K);
+  auto it = e.bgraphs.find(key);
+  if (it != e.bgraphs.end()) {
+    *out = it->second;
+    return IAM_OK;
+  }
+  E_CUDA(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
+  const int r = enqueue_step(e, n_seq, K);
+  cudaGraph_t gg = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(e.stream, &gg);
+  if (r != IAM_OK) {
+    if (gg) cudaGraphDestroy(gg);
+    return r;
+  }
+  E_CUDA(ce);
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&ex, gg, 0);
+  cudaGraphDestroy(gg);
+  E_CUDA(ie);
+  e.bgraphs[key] = ex;
   *out = ex;
   return IAM_OK;
 }
@@ -896,6 +1000,7 @@ extern "C" void iam_dims_qwen35_27b(iam_dims* d) {
   d->eps = 1e-6f;
   d->max_ctx = 4608;
   d->max_rows = 128;
+  d->max_seqs = 1;
 }
 
 static int validate_dims(const iam_dims& d, int world) {
@@ -915,7 +1020,8 @@ static int validate_dims(const iam_dims& d, int world) {
             "dims: at most 8 query heads per KV head per GPU");
   IAM_CHECK(d.intermediate % (64 * world) == 0, "dims: intermediate / world must be a multiple of 64");
   IAM_CHECK(d.vocab % (16 * world) == 0, "dims: vocab / world must be a multiple of 16");
-  IAM_CHECK(d.max_rows >= 1 && d.max_rows <= iam::kMaxRowsFinalize, "dims: max_rows in 1..256");
+  IAM_CHECK(d.max_rows >= 1 && d.max_rows <= 4096, "dims: max_rows in 1..4096");
+  IAM_CHECK(d.max_seqs >= 1 && d.max_seqs <= d.max_rows && d.max_seqs <= 65535, "dims: max_seqs in 1..max_rows");
   IAM_CHECK(d.max_ctx >= d.max_rows, "dims: max_ctx");
   return IAM_OK;
 }
@@ -993,14 +1099,17 @@ extern "C" void iam_destroy(iam_engine* eng) {
   if (e.stream) cudaStreamSynchronize(e.stream);
   for (auto& kv : e.graphs) cudaGraphExecDestroy(kv.second);
   e.graphs.clear();
+  for (auto& kv : e.bgraphs) cudaGraphExecDestroy(kv.second);
+  e.bgraphs.clear();
   if (e.comm) iam::nccl_destroy(e.comm);
   void* bufs[] = {e.pool, e.ppool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
                   e.mid, e.mlp_h, e.q_buf, e.part_o, e.part_ml, e.red32, e.keys, e.best, e.rope_cs, e.d_in, e.d_out,
-                  e.d_err, e.qws, e.qctr, e.gin};
+                  e.d_err, e.qws, e.qctr, e.gin, e.d_bin, e.d_bout};
   for (void* p : bufs)
     if (p) cudaFree(p);
-  if (e.h_in) cudaFreeHost(e.h_in);
-  if (e.h_out) cudaFreeHost(e.h_out);
+  for (void* p : {static_cast<void*>(e.h_in), static_cast<void*>(e.h_out), static_cast<void*>(e.h_bin),
+                  static_cast<void*>(e.h_bout)})
+    if (p) cudaFreeHost(p);
   if (e.stream) cudaStreamDestroy(e.stream);
   delete eng;
 }
@@ -1347,36 +1456,47 @@ extern "C" int iam_read_tensor(iam_engine* eng, const char* name, void* host_ptr
   E_CUDA(cudaSetDevice(e.device));
   E_CUDA(cudaStreamSynchronize(e.stream));
   const std::string n(name);
-  const void* src = nullptr;
-  size_t have = 0;
   auto it = e.by_name.find(n);
   if (it != e.by_name.end()) {
-    src = e.tensors[it->second].ptr;
-    have = e.tensors[it->second].bytes();
-  } else if (n.rfind("state.S.", 0) == 0 || n.rfind("state.conv.", 0) == 0 || n.rfind("state.k_cache.", 0) == 0 ||
-             n.rfind("state.v_cache.", 0) == 0) {
-    const int li = std::atoi(n.substr(n.rfind('.') + 1).c_str());
-    if (li < 0 || li >= e.d.n_layers) return e.setf(IAM_EINVAL, "iam_read_tensor: layer out of range");
-    const Layer& L = e.layers[li];
-    if (n.rfind("state.S.", 0) == 0 && !L.attn) {
-      int par = 0;
-      E_CUDA(cudaMemcpy(&par, e.d_parity, sizeof(int), cudaMemcpyDeviceToHost));
-      have = static_cast<size_t>(e.gv_l) * e.d.gdn_dk * e.d.gdn_dv * 4;
-      src = e.S + (par ? e.s_half : 0) + static_cast<size_t>(L.idx) * e.gv_l * e.d.gdn_dk * e.d.gdn_dv;
-    } else if (n.rfind("state.conv.", 0) == 0 && !L.attn) {
-      int par = 0;
-      E_CUDA(cudaMemcpy(&par, e.d_parity, sizeof(int), cudaMemcpyDeviceToHost));
-      have = static_cast<size_t>(3) * e.conv_l * 2;
-      src = e.conv[par] + static_cast<size_t>(L.idx) * 3 * e.conv_l;
-    } else if (L.attn) {
-      have = static_cast<size_t>(e.d.max_ctx) * e.hkv_l * e.d.head_dim * 2;
-      src = (n.rfind("state.k_cache.", 0) == 0 ? e.kc : e.vc) + static_cast<size_t>(L.idx) * e.d.max_ctx * e.hkv_l *
-                                                                    e.d.head_dim;
-    }
+    if (bytes > e.tensors[it->second].bytes())
+      return e.setf(IAM_EINVAL, "iam_read_tensor: more bytes requested than the tensor holds");
+    E_CUDA(cudaMemcpy(host_ptr, e.tensors[it->second].ptr, bytes, cudaMemcpyDeviceToHost));
+    return IAM_OK;
   }
-  if (!src) return e.setf(IAM_EINVAL, std::string("iam_read_tensor: unknown tensor ") + n);
-  if (bytes > have) return e.setf(IAM_EINVAL, "iam_read_tensor: more bytes requested than the tensor holds");
-  E_CUDA(cudaMemcpy(host_ptr, src, bytes, cudaMemcpyDeviceToHost));
+  const bool isS = n.rfind("state.S.", 0) == 0, isC = n.rfind("state.conv.", 0) == 0;
+  const bool isK = n.rfind("state.k_cache.", 0) == 0, isV = n.rfind("state.v_cache.", 0) == 0;
+  if (!(isS || isC || isK || isV)) return e.setf(IAM_EINVAL, std::string("iam_read_tensor: unknown tensor ") + n);
+  const int li = std::atoi(n.substr(n.rfind('.') + 1).c_str());
+  if (li < 0 || li >= e.d.n_layers) return e.setf(IAM_EINVAL, "iam_read_tensor: layer out of range");
+  const Layer& L = e.layers[li];
+  if ((isS || isC) == L.attn) return e.setf(IAM_EINVAL, std::string("iam_read_tensor: layer has no ") + n);
+  // every slot, slot after slot; the GDN state and conv window of a slot from
+  // the copy its parity word names
+  size_t per = 0;
+  std::vector<int> par(static_cast<size_t>(e.max_seqs), 0);
+  if (isS || isC) E_CUDA(cudaMemcpy(par.data(), e.d_parity, sizeof(int) * e.max_seqs, cudaMemcpyDeviceToHost));
+  if (isS) per = e.s_per * 4;
+  else if (isC) per = static_cast<size_t>(3) * e.conv_l * 2;
+  else per = static_cast<size_t>(e.d.max_ctx) * e.hkv_l * e.d.head_dim * 2;
+  if (bytes > per * e.max_seqs) return e.setf(IAM_EINVAL, "iam_read_tensor: more bytes requested than the tensor holds");
+  char* dst = static_cast<char*>(host_ptr);
+  for (int q = 0; q < e.max_seqs && bytes > 0; ++q) {
+    const char* src = nullptr;
+    if (isS)
+      src = reinterpret_cast<const char*>(e.S + (par[q] ? e.s_half : 0) +
+                                          (static_cast<size_t>(L.idx) * e.max_seqs + q) * e.s_per);
+    else if (isC)
+      src = reinterpret_cast<const char*>(e.conv[par[q]] +
+                                          (static_cast<size_t>(L.idx) * e.max_seqs + q) * 3 * e.conv_l);
+    else
+      src = reinterpret_cast<const char*>((isK ? e.kc : e.vc) +
+                                          (static_cast<size_t>(L.idx) * e.max_seqs + q) * e.d.max_ctx * e.hkv_l *
+                                              e.d.head_dim);
+    const size_t nb = std::min(bytes, per);
+    E_CUDA(cudaMemcpy(dst, src, nb, cudaMemcpyDeviceToHost));
+    dst += nb;
+    bytes -= nb;
+  }
   return IAM_OK;
 }
 
@@ -1396,18 +1516,27 @@ extern "C" int iam_state_reset(iam_engine* eng) {
   IAM_CHECK(eng, "iam_state_reset: null engine");
   EngineImpl& e = eng->impl;
   E_CUDA(cudaSetDevice(e.device));
+  const size_t slots = static_cast<size_t>(e.max_seqs);
   if (e.s_half) E_CUDA(cudaMemsetAsync(e.S, 0, 2 * e.s_half * sizeof(float), e.stream));
   for (int i = 0; i < 2; ++i)
-    if (e.n_gdn) E_CUDA(cudaMemsetAsync(e.conv[i], 0, static_cast<size_t>(e.n_gdn) * 3 * e.conv_l * 2, e.stream));
-  const size_t kv = static_cast<size_t>(e.n_attn) * e.d.max_ctx * e.hkv_l * e.d.head_dim * 2;
+    if (e.n_gdn)
+      E_CUDA(cudaMemsetAsync(e.conv[i], 0, static_cast<size_t>(e.n_gdn) * slots * 3 * e.conv_l * 2, e.stream));
+  const size_t kv = static_cast<size_t>(e.n_attn) * slots * e.d.max_ctx * e.hkv_l * e.d.head_dim * 2;
   if (kv) {
     E_CUDA(cudaMemsetAsync(e.kc, 0, kv, e.stream));
     E_CUDA(cudaMemsetAsync(e.vc, 0, kv, e.stream));
   }
-  E_CUDA(cudaMemsetAsync(e.d_parity, 0, sizeof(int), e.stream));
+  E_CUDA(cudaMemsetAsync(e.d_parity, 0, slots * sizeof(int), e.stream));
+  E_CUDA(cudaMemsetAsync(e.d_bin, 0, slots * sizeof(int32_t), e.stream));
   E_CUDA(cudaStreamSynchronize(e.stream));
   e.last_K = 0;
   return IAM_OK;
+}
+
+// Synthetic-stream name of a state tensor of sequence slot q: slot 0 keeps
+// the single-sequence names, slot q > 0 appends ".s<q>".
+static std::string state_name(const std::string& base, int q) {
+  return q ? base + ".s" + std::to_string(q) : base;
 }
 
 extern "C" int iam_state_init(iam_engine* eng, uint64_t seed, int ctx) {
@@ -1427,49 +1556,52 @@ extern "C" int iam_state_init(iam_engine* eng, uint64_t seed, int ctx) {
   for (const Layer& L : e.layers) {
     const int li = static_cast<int>(&L - e.layers.data());
     const std::string ls = std::to_string(li);
-    if (L.attn) {
-      if (ctx == 0) continue;
-      for (int kvsel = 0; kvsel < 2; ++kvsel) {
+    for (int q = 0; q < e.max_seqs; ++q) {
+      const size_t slot = static_cast<size_t>(L.idx) * e.max_seqs + q;
+      if (L.attn) {
+        if (ctx == 0) continue;
+        for (int kvsel = 0; kvsel < 2; ++kvsel) {
+          SynthJob j = {};
+          j.stream = synth_stream(seed, state_name(std::string(kvsel ? "state.v_cache." : "state.k_cache.") + ls, q).c_str());
+          j.kind = SYN_NORMAL_BF16;
+          j.p0 = 1.0f;
+          j.full_cols = static_cast<uint64_t>(d.n_kv_heads) * d.head_dim;
+          j.row0 = 0;
+          j.rows = static_cast<uint64_t>(ctx);
+          j.col0 = static_cast<uint64_t>(e.kv0) * d.head_dim;
+          j.width = static_cast<uint64_t>(e.hkv_l) * d.head_dim;
+          j.dst = (kvsel ? e.vc : e.kc) + slot * d.max_ctx * e.hkv_l * d.head_dim;
+          E_RUN(synth_fill(j, e.stream));
+        }
+      } else {
         SynthJob j = {};
-        j.stream = synth_stream(seed, (std::string(kvsel ? "state.v_cache." : "state.k_cache.") + ls).c_str());
+        j.stream = synth_stream(seed, state_name("state.conv." + ls, q).c_str());
         j.kind = SYN_NORMAL_BF16;
         j.p0 = 1.0f;
-        j.full_cols = static_cast<uint64_t>(d.n_kv_heads) * d.head_dim;
+        j.full_cols = static_cast<uint64_t>(conv_dim);
         j.row0 = 0;
-        j.rows = static_cast<uint64_t>(ctx);
-        j.col0 = static_cast<uint64_t>(e.kv0) * d.head_dim;
-        j.width = static_cast<uint64_t>(e.hkv_l) * d.head_dim;
-        j.dst = (kvsel ? e.vc : e.kc) + static_cast<size_t>(L.idx) * d.max_ctx * e.hkv_l * d.head_dim;
-        E_RUN(synth_fill(j, e.stream));
+        j.rows = 3;
+        j.dst_ld = static_cast<uint64_t>(e.conv_l);
+        int local = 0;
+        for (auto& c : cr) {
+          j.col0 = static_cast<uint64_t>(c.first);
+          j.width = static_cast<uint64_t>(c.second);
+          j.dst = e.conv[0] + slot * 3 * e.conv_l + local;
+          E_RUN(synth_fill(j, e.stream));
+          local += c.second;
+        }
+        SynthJob sj = {};
+        sj.stream = synth_stream(seed, state_name("state.S." + ls, q).c_str());
+        sj.kind = SYN_NORMAL_F32;
+        sj.p0 = 0.01f;
+        sj.full_cols = static_cast<uint64_t>(d.gdn_dk) * d.gdn_dv;
+        sj.row0 = static_cast<uint64_t>(e.v0);
+        sj.rows = static_cast<uint64_t>(e.gv_l);
+        sj.col0 = 0;
+        sj.width = sj.full_cols;
+        sj.dst = e.S + slot * e.s_per;
+        E_RUN(synth_fill(sj, e.stream));
       }
-    } else {
-      SynthJob j = {};
-      j.stream = synth_stream(seed, ("state.conv." + ls).c_str());
-      j.kind = SYN_NORMAL_BF16;
-      j.p0 = 1.0f;
-      j.full_cols = static_cast<uint64_t>(conv_dim);
-      j.row0 = 0;
-      j.rows = 3;
-      j.dst_ld = static_cast<uint64_t>(e.conv_l);
-      int local = 0;
-      for (auto& c : cr) {
-        j.col0 = static_cast<uint64_t>(c.first);
-        j.width = static_cast<uint64_t>(c.second);
-        j.dst = e.conv[0] + static_cast<size_t>(L.idx) * 3 * e.conv_l + local;
-        E_RUN(synth_fill(j, e.stream));
-        local += c.second;
-      }
-      SynthJob s = {};
-      s.stream = synth_stream(seed, ("state.S." + ls).c_str());
-      s.kind = SYN_NORMAL_F32;
-      s.p0 = 0.01f;
-      s.full_cols = static_cast<uint64_t>(d.gdn_dk) * d.gdn_dv;
-      s.row0 = static_cast<uint64_t>(e.v0);
-      s.rows = static_cast<uint64_t>(e.gv_l);
-      s.col0 = 0;
-      s.width = s.full_cols;
-      s.dst = e.S + static_cast<size_t>(L.idx) * e.gv_l * d.gdn_dk * d.gdn_dv;
-      E_RUN(synth_fill(s, e.stream));
     }
   }
   E_CUDA(cudaStreamSynchronize(e.stream));
@@ -1480,7 +1612,7 @@ static int verify_common(iam_engine* eng, int K, int pos) {
   using namespace iam;
   IAM_CHECK(eng, "iam_verify: null engine");
   EngineImpl& e = eng->impl;
-  IAM_CHECK(K >= 1 && K <= e.d.max_rows, "iam_verify: K out of range (1..max_rows)");
+  IAM_CHECK(K >= 1 && K <= e.d.max_rows && K <= kMaxRowsFinalize, "iam_verify: K out of range (1..max_rows, <= 256)");
   IAM_CHECK(pos >= 0 && pos + K <= e.d.max_ctx, "iam_verify: pos + K exceeds max_ctx");
   E_CUDA(cudaSetDevice(e.device));
   E_RUN(ensure_packed(e));
@@ -1557,7 +1689,8 @@ extern "C" int iam_verify_device(iam_engine* eng, const int32_t* d_tokens, int K
   using namespace iam;
   IAM_CHECK(eng, "iam_verify_device: null engine");
   EngineImpl& e = eng->impl;
-  if (K < 1 || K > e.d.max_rows) return e.setf(IAM_EINVAL, "iam_verify_device: K out of range (1..max_rows)");
+  if (K < 1 || K > e.d.max_rows || K > kMaxRowsFinalize)
+    return e.setf(IAM_EINVAL, "iam_verify_device: K out of range (1..max_rows, <= 256)");
   cudaStream_t st = stream ? as_stream(stream) : e.stream;
   cudaGraphExec_t g = nullptr;
   E_RUN(get_graph(e, K, &g));
@@ -1593,6 +1726,70 @@ extern "C" int iam_rollback(iam_engine* eng, int n_keep, void* stream) {
   return IAM_OK;
 }
 
+static int batch_common(iam_engine* eng, int n_seq, int K) {
+  using namespace iam;
+  IAM_CHECK(eng, "iam_verify_batch: null engine");
+  EngineImpl& e = eng->impl;
+  if (n_seq < 1 || n_seq > e.max_seqs) return e.setf(IAM_EINVAL, "iam_verify_batch: n_seq out of range (1..max_seqs)");
+  if (K < 1 || static_cast<long long>(n_seq) * K > e.d.max_rows)
+    return e.setf(IAM_EINVAL, "iam_verify_batch: n_seq * K exceeds max_rows");
+  E_CUDA(cudaSetDevice(e.device));
+  E_RUN(ensure_packed(e));
+  return IAM_OK;
+}
+
+extern "C" int iam_verify_batch(iam_engine* eng, const int32_t* tokens, int n_seq, int K, const int32_t* pos,
+                                int32_t* argmax_out, int32_t* accept_len) {
+  using namespace iam;
+  int r = batch_common(eng, n_seq, K);
+  if (r != IAM_OK) return r;
+  EngineImpl& e = eng->impl;
+  IAM_CHECK(tokens && pos && argmax_out, "iam_verify_batch: null buffer");
+  const int rows = n_seq * K;
+  for (int q = 0; q < n_seq; ++q)
+    if (pos[q] < 0 || pos[q] + K > e.d.max_ctx) return e.setf(IAM_EINVAL, "iam_verify_batch: pos + K exceeds max_ctx");
+  for (int i = 0; i < rows; ++i)
+    if (tokens[i] < 0 || tokens[i] >= e.d.vocab) return e.setf(IAM_EINVAL, "iam_verify_batch: token id out of range");
+  cudaGraphExec_t g = nullptr;
+  E_RUN(get_batch_graph(e, n_seq, K, &g));
+  // positions of slots 0..n_seq-1, then the tokens right after the slot table
+  std::memcpy(e.h_bin, pos, sizeof(int32_t) * n_seq);
+  std::memcpy(e.h_bin + e.max_seqs, tokens, sizeof(int32_t) * rows);
+  E_CUDA(cudaMemcpyAsync(e.d_bin, e.h_bin, sizeof(int32_t) * n_seq, cudaMemcpyHostToDevice, e.stream));
+  E_CUDA(cudaMemcpyAsync(e.d_bin + e.max_seqs, e.h_bin + e.max_seqs, sizeof(int32_t) * rows, cudaMemcpyHostToDevice,
+                         e.stream));
+  E_CUDA(cudaGraphLaunch(g, e.stream));
+  e.last_K = 0;  // slot 0 advanced outside the single-sequence path: nothing to roll back
+  E_CUDA(cudaMemcpyAsync(e.h_bout, e.d_bout, sizeof(int32_t) * n_seq, cudaMemcpyDeviceToHost, e.stream));
+  E_CUDA(cudaMemcpyAsync(e.h_bout + e.max_seqs, e.d_bout + e.max_seqs, sizeof(int32_t) * rows,
+                         cudaMemcpyDeviceToHost, e.stream));
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  std::memcpy(argmax_out, e.h_bout + e.max_seqs, sizeof(int32_t) * rows);
+  if (accept_len) std::memcpy(accept_len, e.h_bout, sizeof(int32_t) * n_seq);
+  return IAM_OK;
+}
+
+extern "C" int iam_verify_batch_device(iam_engine* eng, const int32_t* d_tokens, int n_seq, int K,
+                                       const int32_t* d_pos, int32_t* d_argmax, int32_t* d_accept, void* stream) {
+  using namespace iam;
+  int r = batch_common(eng, n_seq, K);
+  if (r != IAM_OK) return r;
+  EngineImpl& e = eng->impl;
+  cudaStream_t st = stream ? as_stream(stream) : e.stream;
+  cudaGraphExec_t g = nullptr;
+  E_RUN(get_batch_graph(e, n_seq, K, &g));
+  const int rows = n_seq * K;
+  if (d_pos) E_CUDA(cudaMemcpyAsync(e.d_bin, d_pos, sizeof(int32_t) * n_seq, cudaMemcpyDeviceToDevice, st));
+  if (d_tokens)
+    E_CUDA(cudaMemcpyAsync(e.d_bin + e.max_seqs, d_tokens, sizeof(int32_t) * rows, cudaMemcpyDeviceToDevice, st));
+  E_CUDA(cudaGraphLaunch(g, st));
+  e.last_K = 0;
+  if (d_argmax)
+    E_CUDA(cudaMemcpyAsync(d_argmax, e.d_bout + e.max_seqs, sizeof(int32_t) * rows, cudaMemcpyDeviceToDevice, st));
+  if (d_accept) E_CUDA(cudaMemcpyAsync(d_accept, e.d_bout, sizeof(int32_t) * n_seq, cudaMemcpyDeviceToDevice, st));
+  return IAM_OK;
+}
+
 extern "C" int iam_read_hidden(iam_engine* eng, uint16_t* host_ptr, int K) {
   using namespace iam;
   IAM_CHECK(eng && host_ptr && K >= 1, "iam_read_hidden: bad argument");
@@ -1617,20 +1814,28 @@ extern "C" int iam_step_launches(iam_engine* eng, int K) {
   return e.launches - before;
 }
 
-extern "C" double iam_step_bytes(iam_engine* eng, int K, int pos) {
-  if (!eng) return 0.0;
-  EngineImpl& e = eng->impl;
+// Weights once, plus per sequence its K embedding rows, state read + write
+// and KV read.
+static double step_bytes(const iam::EngineImpl& e, int n_seq, int K, int pos) {
   const iam_dims& d = e.d;
   double w = 0.0;
   for (const auto& t : e.tensors) {
     if (t.name == "model.embed_tokens.weight") continue;
     w += static_cast<double>(t.bytes());
   }
-  w += static_cast<double>(K) * d.hidden * 2;                                            // embedding rows
-  w += 2.0 * e.n_gdn * e.gv_l * d.gdn_dk * d.gdn_dv * 4;                                 // S read + write
-  w += 2.0 * e.n_gdn * 3 * e.conv_l * 2;                                                 // conv state
-  w += 2.0 * e.n_attn * static_cast<double>(pos + K) * e.hkv_l * d.head_dim * 2;         // KV read
-  return w;
+  double q = static_cast<double>(K) * d.hidden * 2;                                      // embedding rows
+  q += 2.0 * e.n_gdn * e.gv_l * d.gdn_dk * d.gdn_dv * 4;                                 // S read + write
+  q += 2.0 * e.n_gdn * 3 * e.conv_l * 2;                                                 // conv state
+  q += 2.0 * e.n_attn * static_cast<double>(pos + K) * e.hkv_l * d.head_dim * 2;         // KV read
+  return w + n_seq * q;
+}
+
+extern "C" double iam_step_bytes(iam_engine* eng, int K, int pos) {
+  return eng ? step_bytes(eng->impl, 1, K, pos) : 0.0;
+}
+
+extern "C" double iam_step_bytes_batch(iam_engine* eng, int n_seq, int K, int pos) {
+  return eng ? step_bytes(eng->impl, n_seq, K, pos) : 0.0;
 }
 
 extern "C" int iam_profile_step(iam_engine* eng, int K, int pos, int cap, const char** kinds, double* ms,
@@ -1644,7 +1849,7 @@ extern "C" int iam_profile_step(iam_engine* eng, int K, int pos, int cap, const 
   e.h_in->pos = pos;
   if (cudaMemcpyAsync(&e.d_in->pos, &e.h_in->pos, 4, cudaMemcpyHostToDevice, e.stream) != cudaSuccess) return -IAM_ECUDA;
   e.prof = &ents;
-  r = enqueue_step(e, K);
+  r = enqueue_step(e, 0, K);
   e.prof = nullptr;
   if (r != IAM_OK) return -r;
   if (cudaStreamSynchronize(e.stream) != cudaSuccess) return -IAM_ECUDA;

@@ -157,7 +157,8 @@ __device__ __forceinline__ void store_state(const float (&S)[RPW][4], float* Sh,
 // head's q^, k^ and its own v rows, runs the recurrence on its rows, and the
 // gated norm's sum of squares over dv is exchanged through distributed
 // shared memory (summed in rank order).  C = 1 is the one-CTA-a-head kernel.
-template <int C>
+// kSeq: one launch over several sequences, grid.y = sequence (GdnArgs n_seq).
+template <int C, bool kSeq>
 __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a) {
   constexpr int R = kHD / C, RPW = R / (kThreads / 32);
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -167,12 +168,22 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rep = a.n_v_heads / a.n_k_heads;
   const int kh = h / rep;
-  const bool swap = a.parity_dev && __ldcg(a.parity_dev);
-  float* S_rd = a.S;
-  float* S_wr = a.S_alt ? a.S_alt : a.S;
+  const int sq = kSeq ? static_cast<int>(blockIdx.y) : 0;
+  const uint16_t* in = a.in;
+  uint16_t* out = a.out;
+  size_t soff = 0, coff = 0;
+  if constexpr (kSeq) {
+    in += static_cast<size_t>(sq) * a.rows * a.ld_in;
+    out += static_cast<size_t>(sq) * a.rows * a.ld_out;
+    soff = static_cast<size_t>(sq) * a.seq_S;
+    coff = static_cast<size_t>(sq) * a.seq_conv;
+  }
+  const bool swap = a.parity_dev && __ldcg(a.parity_dev + sq);
+  float* S_rd = a.S + soff;
+  float* S_wr = (a.S_alt ? a.S_alt : a.S) + soff;
   if (swap && a.S_alt) {
-    S_rd = a.S_alt;
-    S_wr = a.S;
+    S_rd = a.S_alt + soff;
+    S_wr = a.S + soff;
   }
   const size_t hoff = static_cast<size_t>(h) * kHD * kHD;
   const int row0 = jr * R + warp * RPW;  // this warp's first state row
@@ -182,8 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   load_state<RPW>(S, S_rd + hoff, row0, lane);
   pdl_wait();
   pdl_trigger();
-  const uint16_t* conv_in = swap ? a.conv_out : a.conv_in;
-  uint16_t* conv_out = swap ? const_cast<uint16_t*>(a.conv_in) : a.conv_out;
+  const uint16_t* conv_in = (swap ? a.conv_out : a.conv_in) + coff;
+  uint16_t* conv_out = (swap ? const_cast<uint16_t*>(a.conv_in) : a.conv_out) + coff;
 
   // conv channel of this thread: 0..127 q (K-head kh), 128..255 k, then this
   // CTA's R v rows (V-head h)
@@ -223,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
       uint16_t xin[kChunk];
 #pragma unroll
       for (int t = 0; t < kChunk; ++t)
-        xin[t] = t < n ? a.in[static_cast<size_t>(t0 + t) * a.ld_in + col] : uint16_t(0);
+        xin[t] = t < n ? in[static_cast<size_t>(t0 + t) * a.ld_in + col] : uint16_t(0);
 #pragma unroll
       for (int t = 0; t < kChunk; ++t) {
         if (t < n) {
@@ -244,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
       const int t = ct - 384;
       const size_t row = static_cast<size_t>(t0 + t) * a.ld_in;
       float gv, bv;
-      g_beta(bf2f(a.in[row + a.a_col + h]), bf2f(a.in[row + a.b_col + h]), a.A_log[h], bf2f(a.dt_bias[h]), gv, bv);
+      g_beta(bf2f(in[row + a.a_col + h]), bf2f(in[row + a.b_col + h]), a.A_log[h], bf2f(a.dt_bias[h]), gv, bv);
       sm.g[t] = gv;
       sm.beta[t] = bv;
     }
@@ -294,13 +305,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
         const float rms = sqrtf(ss / 128.f + a.eps);
         const size_t row = static_cast<size_t>(t0 + t);
         const int d0 = jr * R + 4 * lane;
-        const uint2 zz = *reinterpret_cast<const uint2*>(a.in + row * a.ld_in + a.z_col + h * kHD + d0);
+        const uint2 zz = *reinterpret_cast<const uint2*>(in + row * a.ld_in + a.z_col + h * kHD + d0);
         const uint2 ww = *reinterpret_cast<const uint2*>(a.norm_w + d0);
         const float o0 = silu_f(lo_bf(zz.x)) * ((y.x / rms) * lo_bf(ww.x));
         const float o1 = silu_f(hi_bf(zz.x)) * ((y.y / rms) * hi_bf(ww.x));
         const float o2 = silu_f(lo_bf(zz.y)) * ((y.z / rms) * lo_bf(ww.y));
         const float o3 = silu_f(hi_bf(zz.y)) * ((y.w / rms) * hi_bf(ww.y));
-        *reinterpret_cast<uint2*>(a.out + row * a.ld_out + h * kHD + d0) =
+        *reinterpret_cast<uint2*>(out + row * a.ld_out + h * kHD + d0) =
             make_uint2(pack_bf2(o0, o1), pack_bf2(o2, o3));
       }
     }
@@ -365,10 +376,10 @@ int ensure_attrs() { return gdn_init_attrs(); }
 
 int gdn_init_attrs() {
   if (g_attr_done) return IAM_OK;
-  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
-  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
-  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
-  IAM_CUDA(cudaFuncSetAttribute(gdn_fused_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
+  for (auto* k : {gdn_fused_kernel<1, false>, gdn_fused_kernel<2, false>, gdn_fused_kernel<4, false>,
+                  gdn_fused_kernel<8, false>, gdn_fused_kernel<1, true>, gdn_fused_kernel<2, true>,
+                  gdn_fused_kernel<4, true>, gdn_fused_kernel<8, true>})
+    IAM_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
   int dev = 0;
   IAM_CUDA(cudaGetDevice(&dev));
   IAM_CUDA(cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -377,10 +388,10 @@ int gdn_init_attrs() {
   return IAM_OK;
 }
 
-template <int C>
+template <int C, bool kSeq>
 int launch_gdn_c(const GdnArgs& a, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.n_v_heads * C);
+  cfg.gridDim = dim3(a.n_v_heads * C, kSeq ? a.n_seq : 1);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = sizeof(GdnSmem);
   cfg.stream = st;
@@ -400,7 +411,7 @@ int launch_gdn_c(const GdnArgs& a, cudaStream_t st, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  IAM_CUDA(cudaLaunchKernelEx(&cfg, gdn_fused_kernel<C>, a));
+  IAM_CUDA(cudaLaunchKernelEx(&cfg, gdn_fused_kernel<C, kSeq>, a));
   return IAM_OK;
 }
 
@@ -427,17 +438,31 @@ int launch_gdn(const GdnArgs& a, cudaStream_t st, bool pdl) {
                 (!a.S_alt || aligned16(a.S_alt)),
             "gdn: 8-byte aligned rows required");
   IAM_CHECK(a.S_alt != a.S, "gdn: the second state buffer must differ from the first");
+  IAM_CHECK(a.n_seq <= 1 || (a.seq_S % 4 == 0 && a.seq_conv > 0 && a.n_seq <= 65535),
+            "gdn: sequence strides (state 16-byte aligned) and 1..65535 sequences required");
   const int r = ensure_attrs();
   if (r != IAM_OK) return r;
+  if (a.n_seq > 1) {
+    switch (gdn_split(a.n_v_heads * a.n_seq, a.rows)) {
+      case 8:
+        return launch_gdn_c<8, true>(a, st, pdl);
+      case 4:
+        return launch_gdn_c<4, true>(a, st, pdl);
+      case 2:
+        return launch_gdn_c<2, true>(a, st, pdl);
+      default:
+        return launch_gdn_c<1, true>(a, st, pdl);
+    }
+  }
   switch (gdn_split(a.n_v_heads, a.rows)) {
     case 8:
-      return launch_gdn_c<8>(a, st, pdl);
+      return launch_gdn_c<8, false>(a, st, pdl);
     case 4:
-      return launch_gdn_c<4>(a, st, pdl);
+      return launch_gdn_c<4, false>(a, st, pdl);
     case 2:
-      return launch_gdn_c<2>(a, st, pdl);
+      return launch_gdn_c<2, false>(a, st, pdl);
     default:
-      return launch_gdn_c<1>(a, st, pdl);
+      return launch_gdn_c<1, false>(a, st, pdl);
   }
 }
 

@@ -43,6 +43,13 @@ int launch_finalize(const unsigned long long* keys, int nparts, int key_ld, int 
 // best[row] = the best key over parts (tensor-parallel partial of finalize)
 int launch_best_keys(const unsigned long long* keys, int nparts, int key_ld, int M, unsigned long long* best,
                      cudaStream_t st, bool pdl);
+// Several sequences of seq_rows rows each: per-row argmax (one CTA a row),
+// then each sequence's accept length.
+int launch_finalize_batch(const unsigned long long* keys, int nparts, int key_ld, int n_seq, int seq_rows,
+                          const int32_t* tokens, int32_t* argmax_out, int32_t* accept, cudaStream_t st, bool pdl);
+// Per-row best key over nparts partial keys, one CTA a row (multi-sequence TP).
+int launch_best_rows(const unsigned long long* keys, int nparts, int key_ld, int M, unsigned long long* best,
+                     cudaStream_t st, bool pdl);
 
 // GatedDeltaNet fused step (gdn.cu)
 struct GdnArgs {
@@ -61,8 +68,14 @@ struct GdnArgs {
   int ld_out;
   int n_k_heads, n_v_heads;  // heads handled by this launch (shard-local)
   int key_dim, conv_dim;     // shard-local widths of the qkv block
-  int rows;
+  int rows;                  // tokens of one sequence
   float eps;
+  // Several sequences in one launch (grid.y = n_seq; 0 or 1: one): sequence
+  // q reads input rows [q * rows, (q + 1) * rows) of `in`, writes the same rows
+  // of `out`, and its state, conv windows and parity word sit seq_S floats,
+  // seq_conv elements and q ints past those of sequence 0.
+  int n_seq;
+  size_t seq_S, seq_conv;
   const int* parity_dev;  // optional: when *parity_dev == 1, conv_in/conv_out (and S/S_alt) swap roles;
                           // read before the grid-dependency wait, so only a kernel launched without
                           // programmatic overlap may have written it
@@ -85,9 +98,14 @@ struct AttnArgs {
   int n_heads, n_kv_heads, head_dim, rotary_dim;
   const float* rope_cs;  // [max_ctx, rotary/2, 2] cos/sin
   int max_ctx;
-  int rows;
+  int rows;             // all rows of the launch
   int pos;              // position of row 0 (ignored when pos_dev is set)
-  const int* pos_dev;   // device position (graph replay)
+  const int* pos_dev;   // device position (graph replay); one per sequence when n_seq > 1
+  // Several sequences in one launch (0 or 1: one): rows [q * seq_rows,
+  // (q + 1) * seq_rows) belong to sequence q, whose caches sit q * seq_kv
+  // elements past k_cache / v_cache and whose position is pos_dev[q].
+  int n_seq, seq_rows;
+  size_t seq_kv;
   int chunk;            // context tokens per split
   int nsplit;           // context splits (partials per query head)
   float eps;

@@ -320,6 +320,53 @@ __global__ void __launch_bounds__(1024) best_keys_kernel(const unsigned long lon
   }
 }
 
+// Multi-sequence finalisation, one CTA a row: the row's best key over the
+// nparts partial keys (lm_head tiles, or ranks) -> argmax index, or (best_out)
+// the key itself for the cross-rank reduction.
+__global__ void __launch_bounds__(256) finalize_rows_kernel(const unsigned long long* __restrict__ keys, int nparts,
+                                                            int key_ld, int32_t* argmax_out,
+                                                            unsigned long long* best_out) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ unsigned long long sh[32];
+  const unsigned long long best = best_key_of_row(keys, nparts, key_ld, blockIdx.x, sh);
+  if (threadIdx.x == 0) {
+    if (best_out) best_out[blockIdx.x] = best;
+    else argmax_out[blockIdx.x] = static_cast<int32_t>(argmax_key_index(best));
+  }
+}
+
+// Each sequence's greedy accept length over its seq_rows rows (the rule of
+// finalize_kernel).
+__global__ void accept_kernel(const int32_t* __restrict__ tokens, const int32_t* __restrict__ argmax, int n_seq,
+                              int seq_rows, int32_t* accept) {
+  pdl_wait();
+  pdl_trigger();
+  for (int q = threadIdx.x; q < n_seq; q += blockDim.x) {
+    const int32_t* tk = tokens + static_cast<size_t>(q) * seq_rows;
+    const int32_t* am = argmax + static_cast<size_t>(q) * seq_rows;
+    int j = 0;
+    while (j + 1 < seq_rows && tk[j + 1] == am[j]) ++j;
+    accept[q] = j;
+  }
+}
+
+int launch_finalize_batch(const unsigned long long* keys, int nparts, int key_ld, int n_seq, int seq_rows,
+                          const int32_t* tokens, int32_t* argmax_out, int32_t* accept, cudaStream_t st, bool pdl) {
+  IAM_CHECK(n_seq >= 1 && seq_rows >= 1 && n_seq * seq_rows <= key_ld, "finalize: bad sequence shape");
+  const int r = launch_k(finalize_rows_kernel, dim3(n_seq * seq_rows), dim3(256), 0, st, pdl, keys, nparts, key_ld,
+                         argmax_out, static_cast<unsigned long long*>(nullptr));
+  if (r != IAM_OK) return r;
+  return launch_k(accept_kernel, dim3(1), dim3(256), 0, st, pdl, tokens, static_cast<const int32_t*>(argmax_out),
+                  n_seq, seq_rows, accept);
+}
+
+int launch_best_rows(const unsigned long long* keys, int nparts, int key_ld, int M, unsigned long long* best,
+                     cudaStream_t st, bool pdl) {
+  return launch_k(finalize_rows_kernel, dim3(M), dim3(256), 0, st, pdl, keys, nparts, key_ld,
+                  static_cast<int32_t*>(nullptr), best);
+}
+
 int launch_finalize(const unsigned long long* keys, int nparts, int key_ld, int M, const int32_t* tokens,
                     int32_t* argmax_out, int32_t* accept, cudaStream_t st, bool pdl) {
   IAM_CHECK(M <= kMaxRowsFinalize, "finalize: too many rows");

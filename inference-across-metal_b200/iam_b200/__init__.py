@@ -69,6 +69,9 @@ _SIGS = {
     "iam_profile_step": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "iam_step_launches": (_i, [_vp, _i]),
     "iam_step_bytes": (C.c_double, [_vp, _i, _i]),
+    "iam_step_bytes_batch": (C.c_double, [_vp, _i, _i, _i]),
+    "iam_verify_batch": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "iam_verify_batch_device": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp]),
 }
 
 _LIB = None
@@ -201,7 +204,7 @@ class Dims(C.Structure):
     _fields_ = [(n, C.c_float if n in ("rope_theta", "eps") else C.c_int) for n in (
         "hidden", "intermediate", "vocab", "n_layers", "full_attn_interval", "n_heads", "n_kv_heads", "head_dim",
         "rotary_dim", "rope_theta", "gdn_k_heads", "gdn_v_heads", "gdn_dk", "gdn_dv", "conv_kernel", "group_size",
-        "eps", "max_ctx", "max_rows")]
+        "eps", "max_ctx", "max_rows", "max_seqs")]
 
     @classmethod
     def qwen35_27b(cls, **over):
@@ -315,6 +318,26 @@ class Engine:
 
     def verify_device(self, d_tokens, K: int, pos: int, d_argmax=None, stream=None):
         self._c(lib().iam_verify_device(self._h, d_tokens, K, pos, d_argmax, _s(stream)))
+
+    def verify_batch(self, tokens, pos):
+        """tokens [n_seq, K] (row 0 of each: the token being decoded), pos [n_seq]
+        -> (argmax [n_seq, K], accept_len [n_seq]); sequence q uses slot q."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        n, K = t.shape
+        p = np.ascontiguousarray(pos, dtype=np.int32)
+        am = np.zeros((n, K), np.int32)
+        acc = np.zeros(n, np.int32)
+        self._c(lib().iam_verify_batch(self._h, t.ctypes.data_as(C.c_void_p), n, K, p.ctypes.data_as(C.c_void_p),
+                                       am.ctypes.data_as(C.c_void_p), acc.ctypes.data_as(C.c_void_p)))
+        return am, acc
+
+    def verify_batch_device(self, d_tokens, n_seq: int, K: int, d_pos=None, d_argmax=None, d_accept=None,
+                            stream=None):
+        self._c(lib().iam_verify_batch_device(self._h, d_tokens, n_seq, K, d_pos, d_argmax, d_accept, _s(stream)))
+
+    def step_bytes_batch(self, n_seq: int, K: int, pos: int) -> float:
+        return lib().iam_step_bytes_batch(self._h, n_seq, K, pos)
 
     def read_tensor(self, name: str, nbytes: int):
         import numpy as np

@@ -86,24 +86,31 @@ def make_weights(seed: int, d: Dims, layers=None) -> dict:
     return W
 
 
-def make_state(seed: int, d: Dims, ctx: int, max_ctx: int, layers=None) -> State:
+def state_name(kind: str, li: int, slot: int = 0) -> str:
+    """Synthetic-stream name of a state tensor; sequence slot s > 0 of a
+    multi-sequence engine appends ".s<s>" (slot 0 is the single sequence)."""
+    return f"state.{kind}.{li}" + (f".s{slot}" if slot else "")
+
+
+def make_state(seed: int, d: Dims, ctx: int, max_ctx: int, layers=None, slot: int = 0) -> State:
     """Seeded recurrent state and KV cache for a context of ``ctx`` prior tokens:
     conv state N(0,1) bf16 [3, C]; S N(0, 0.01) fp32 [Hv, dv, dk];
-    KV cache N(0,1) bf16 in positions [0, ctx) of a [max_ctx, Hkv, d] buffer."""
+    KV cache N(0,1) bf16 in positions [0, ctx) of a [max_ctx, Hkv, d] buffer.
+    ``slot`` selects the sequence slot of a multi-sequence engine."""
     conv, S, kc, vc = {}, {}, {}, {}
     for li in (range(d.n_layers) if layers is None else layers):
         if d.is_full_attn(li):
             n = ctx * d.n_kv_heads * d.head_dim
-            for store, tag in ((kc, "k"), (vc, "v")):
+            for store, tag in ((kc, "k_cache"), (vc, "v_cache")):
                 buf = np.zeros((max_ctx, d.n_kv_heads, d.head_dim), np.float32)
                 if n:
-                    buf[:ctx] = synth.gen_normal_bf16(seed, f"state.{tag}_cache.{li}", n, 1.0) \
+                    buf[:ctx] = synth.gen_normal_bf16(seed, state_name(tag, li, slot), n, 1.0) \
                         .astype(np.float32).reshape(ctx, d.n_kv_heads, d.head_dim)
                 store[li] = buf
         else:
-            conv[li] = synth.gen_normal_bf16(seed, f"state.conv.{li}", (d.conv_kernel - 1) * d.conv_dim, 1.0) \
-                .astype(np.float32).reshape(d.conv_kernel - 1, d.conv_dim)
-            S[li] = synth.gen_normal_f32(seed, f"state.S.{li}", d.gdn_v_heads * d.gdn_dv * d.gdn_dk, 0.01) \
+            conv[li] = synth.gen_normal_bf16(seed, state_name("conv", li, slot), (d.conv_kernel - 1) * d.conv_dim,
+                                             1.0).astype(np.float32).reshape(d.conv_kernel - 1, d.conv_dim)
+            S[li] = synth.gen_normal_f32(seed, state_name("S", li, slot), d.gdn_v_heads * d.gdn_dv * d.gdn_dk, 0.01) \
                 .reshape(d.gdn_v_heads, d.gdn_dv, d.gdn_dk).copy()
     return State(conv=conv, S=S, k_cache=kc, v_cache=vc)
 
