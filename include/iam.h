@@ -83,7 +83,7 @@ int iam_qmm_affine4_noalloc(const uint32_t* w, const uint16_t* s, const uint16_t
  *     invalid sizes);
  *   iam_qmm_pack_affine4: w, s, b as for iam_qmm_affine4 -> packed (device
  *     memory of that size, 16-byte aligned), stream-ordered;
- *   iam_qmm_affine4_packed: y = x . W^T, any M >= 1 (passes of 32 tokens). */
+ *   iam_qmm_affine4_packed: y = x . W^T, any M >= 1 (passes of 64 tokens). */
 size_t iam_qmm_packed_bytes(int N, int K);
 int iam_qmm_pack_affine4(const uint32_t* w, const uint16_t* s, const uint16_t* b, void* packed, int N, int K,
                          void* stream);

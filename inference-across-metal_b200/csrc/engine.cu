@@ -453,8 +453,9 @@ int alloc_all(EngineImpl& e) {
   if (e.world > 1) E_CUDA(cudaMalloc(&e.red32, static_cast<size_t>(R) * H * 4));
   e.lm_ctas = ceil_div(e.vocab_l, 16);  // at least 16 rows per CTA in every config
   E_CUDA(cudaMalloc(&e.keys, static_cast<size_t>(e.lm_ctas) * R * 8));
-  // split-K workspace: at most (rows / 16) tiles x 128 floats per token tile of
-  // 32 tokens for the widest matrix (lm_head or the fused projections)
+  // split-K workspace: (rows / 16) tiles x 512 floats for the widest matrix
+  // (lm_head or the fused projections); a plan that would need more runs
+  // with a smaller split (qmm_tc_run caps it by the workspace)
   {
     const size_t widest = std::max<size_t>({static_cast<size_t>(e.vocab_l), static_cast<size_t>(2 * e.inter_l),
                                             static_cast<size_t>(e.ld_in), static_cast<size_t>(e.ld_attn),

@@ -850,7 +850,8 @@ int qmm_op_workspace(int kind, size_t floats, size_t ctrs, cudaStream_t st, floa
   return IAM_OK;
 }
 
-// Validates one matmul and launches it in passes of at most 32 tokens.  A null
+// Validates one matmul and launches it in passes of at most 64 tokens (packed
+// weights, tensor cores) or 32 (MLX layout, mma.sync).  A null
 // a.ws selects the library's own split-K workspace.
 int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap) {
   IAM_CHECK(a.K > 0 && a.K % 64 == 0, "qmm: K must be a positive multiple of 64");
@@ -863,9 +864,9 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
   if (packed) {
     const int total_m = a.M;
     const uint16_t* x0 = a.x;
-    for (int m0 = 0; m0 < total_m; m0 += 32) {
+    for (int m0 = 0; m0 < total_m; m0 += 64) {  // the tensor-core kernel's widest token tile
       QmmArgs p = a;
-      p.M = std::min(32, total_m - m0);
+      p.M = std::min(64, total_m - m0);
       p.x = x0 + static_cast<size_t>(m0) * a.ldx;
       for (int i = 0; i < p.nseg; ++i) {
         QmmSeg& s = p.seg[i];

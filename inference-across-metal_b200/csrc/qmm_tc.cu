@@ -6,7 +6,7 @@
 // batch_verify_27b.swift:100-119), computed on weights re-packed once at load
 // into 128-row x 256-k blocks (qmm.cuh).
 //
-// One CTA per SM owns a 128-row tile of y^T for all tokens of the pass (<= 32)
+// One CTA per SM owns a 128-row tile of y^T for all tokens of the pass (<= 64)
 // over a range of k blocks:
 //  * one thread of warp 0 feeds two shared-memory rings: weight blocks (codes
 //    and (scale, bias) pairs, one contiguous 18 KiB bulk copy a block, freed
@@ -22,8 +22,8 @@
 //    q * scale + bias to bf16 once, the value mx.dequantize produces -- and
 //    store them into a 3-block ring of A operands in tensor memory
 //    (tcgen05.st): the MMA's A operand never passes through shared memory;
-//  * one thread of warp 1 issues tcgen05.mma kind::f16 (M = 128, N = 16 or
-//    32, K = 16; A from tensor memory, B from shared memory) into an fp32
+//  * one thread of warp 1 issues tcgen05.mma kind::f16 (M = 128, N = 16, 32
+//    or 64, K = 16; A from tensor memory, B from shared memory) into an fp32
 //    accumulator in tensor memory; tcgen05.commit hands A slots and
 //    activation stages back.  The tensor core takes about 19 cycles an MMA
 //    at these shapes but a barrier check stalls the issuing thread for 100+,
@@ -53,8 +53,7 @@ constexpr int kTcDqWarps = 16;
 constexpr int kTcThreads = 32 * (2 + kTcDqWarps);
 constexpr int kTcASlots = 3;                         // TMEM A slots of one 256-k block (128 columns)
 constexpr uint32_t kTcTmemCols = 512;
-constexpr uint32_t kTcDCol = 128 * kTcASlots;        // accumulator: NN (<= 32) columns
-static_assert(kTcDCol + 32 <= kTcTmemCols, "TMEM budget");
+constexpr uint32_t kTcDCol = 128 * kTcASlots;        // accumulator: NN (<= 64) columns
 
 constexpr uint32_t kMagic = 0x43004300u;
 constexpr uint32_t kNibMask = 0x000F000Fu;
@@ -139,8 +138,10 @@ struct QmmTcArgs {
 
 template <int NN>
 struct TcLayout {
-  static constexpr int kWS = NN == 16 ? 8 : 7;             // weight ring stages
-  static constexpr int kXS = NN == 16 ? 8 : 6;             // activation ring stages (L2 latency ~1 us)
+  static_assert(NN == 16 || NN == 32 || NN == 64, "token tile");
+  static_assert(kTcDCol + NN <= kTcTmemCols, "TMEM budget");
+  static constexpr int kWS = NN == 16 ? 8 : 7;                        // weight ring stages
+  static constexpr int kXS = NN == 16 ? 8 : NN == 32 ? 6 : 3;         // activation ring stages (L2 latency ~1 us)
   static constexpr int kXBox = NN * 128;                   // one [NN x 64 k] box
   static constexpr int kXBytes = 4 * kXBox;                // 256 k of activations
   static constexpr int kWOff = kXS * kXBytes;              // weight ring after the (1 KiB aligned) x ring
@@ -384,7 +385,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     const bool have = __all_sync(0xffffffffu, mbar_wait_light(dfull, 0));
     if (!have) give_up();
     tc_fence_after();
-    if constexpr (EC == 8) {
+    if constexpr (EC == 16) {
+      tmem_ld16(lane_base + kTcDCol + h * EC, v);
+    } else if constexpr (EC == 8) {
       tmem_ld8(lane_base + kTcDCol + h * EC, v);
     } else {
       tmem_ld4(lane_base + kTcDCol + h * EC, v);
@@ -574,7 +577,7 @@ __global__ void qmm_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* 
 }
 
 int g_tc_sms = 0;
-bool g_tc_attr[2] = {false, false};
+bool g_tc_attr[3] = {false, false, false};
 
 template <int NN>
 void* tc_fn() {
@@ -583,7 +586,7 @@ void* tc_fn() {
 
 template <int NN>
 int tc_occupancy() {
-  const int idx = NN == 16 ? 0 : 1;
+  const int idx = NN == 16 ? 0 : NN == 32 ? 1 : 2;
   if (!g_tc_attr[idx]) {
     cudaFuncSetAttribute(qmm_tc_kernel<NN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<NN>::kSmem);
     g_tc_attr[idx] = true;
@@ -674,7 +677,7 @@ static int tc_launch(const QmmTcArgs& ta, int ks, cudaStream_t st, bool pdl) {
 
 int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap) {
   IAM_CHECK(a.K > 0 && a.K % 64 == 0, "qmm: K must be a positive multiple of 64");
-  IAM_CHECK(a.M >= 1 && a.M <= 32, "qmm: the tensor-core path takes 1..32 tokens a pass");
+  IAM_CHECK(a.M >= 1 && a.M <= 64, "qmm: the tensor-core path takes 1..64 tokens a pass");
   IAM_CHECK(a.nseg >= 1 && a.nseg <= kQmmMaxSeg, "qmm: 1..4 segments");
   IAM_CHECK(aligned16(a.x) && a.ldx % 8 == 0 && a.ldx >= a.K, "qmm: x must be 16-byte aligned with ldx % 8 == 0");
   if (g_tc_sms == 0) {
@@ -695,9 +698,9 @@ int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_
     cta += qp_tiles(s.rows, s.mode == EPI_SWIGLU);
   }
   a.total_ctas = cta;
-  const int NN = a.M <= 16 ? 16 : 32;
+  const int NN = a.M <= 16 ? 16 : a.M <= 32 ? 32 : 64;
   const int KB = qp_kblocks(a.K);
-  const int occ = NN == 16 ? tc_occupancy<16>() : tc_occupancy<32>();
+  const int occ = NN == 16 ? tc_occupancy<16>() : NN == 32 ? tc_occupancy<32>() : tc_occupancy<64>();
   int ks = tc_plan_ks(cta, KB, occ);
   if (ks > 1 && a.ws) {  // a caller's workspace bounds the split
     const size_t per = static_cast<size_t>(cta) * kQpRows * NN;
@@ -720,7 +723,8 @@ int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_
   const int r = tma_encode_2d(&ta.xmap, a.x, 2, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K), NN, 64, true,
                               static_cast<uint64_t>(a.ldx));
   if (r != IAM_OK) return r;
-  return NN == 16 ? tc_launch<16>(ta, ks, st, pdl) : tc_launch<32>(ta, ks, st, pdl);
+  if (NN == 16) return tc_launch<16>(ta, ks, st, pdl);
+  return NN == 32 ? tc_launch<32>(ta, ks, st, pdl) : tc_launch<64>(ta, ks, st, pdl);
 }
 
 }  // namespace iam

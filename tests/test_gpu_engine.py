@@ -152,6 +152,19 @@ def test_tiny_model_verify(K):
     e.close()
 
 
+def test_tiny_model_verify_wide_block():
+    """K = 48: every matmul of the step (fused projections, SwiGLU, residual,
+    lm_head argmax) on the tensor-core kernel's 64-token tile."""
+    d = O.TINY
+    K, pos = 48, 20
+    tokens = SM.draft_tokens(SEED, d, K, tag="tiny_wide")
+    e, am, acc, hid = run_engine(d, tokens, pos, pos, 96, max_rows=64)
+    W, st, am_ref, acc_ref, normed, logits = oracle_step(d, tokens, pos, pos, 96)
+    assert_close_bf16(hid, normed)
+    check_argmax(am, logits)
+    e.close()
+
+
 def test_accept_length_counts_matching_drafts():
     d = O.TINY
     e = I.Engine(cdims(d, 64, 8))

@@ -97,7 +97,7 @@ def test_pack_layout_matches_restatement():
     assert np.array_equal(got, ref)
 
 
-@pytest.mark.parametrize("M", [1, 32])
+@pytest.mark.parametrize("M", [1, 32, 64])
 def test_qmm_packed_mixed_tiles(M):
     """Tiles with a scale >= 0.25 use the general conversion, the others the
     2^130 pre-scaled one; both must match the oracle."""
@@ -131,7 +131,7 @@ def _case(N, K, M, indep_bias=False, seed=31):
 
 
 @pytest.mark.parametrize("N,K", [(10240, 5120), (6144, 5120), (48, 5120), (5120, 6144), (1024, 5120)])
-@pytest.mark.parametrize("M", [1, 3, 8, 16, 17, 32, 40])
+@pytest.mark.parametrize("M", [1, 3, 8, 16, 17, 32, 40, 64, 100])
 def test_qmm_packed_matches_oracle(N, K, M):
     got, ref = _case(N, K, M)
     assert_close_bf16(got, ref)
