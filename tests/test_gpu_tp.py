@@ -78,6 +78,57 @@ def _rank_main(rank, world, port):
         dist.destroy_process_group()
 
 
+def _rank_batch(rank, world, port):
+    """Multi-sequence verify on 2 ranks: per-row lm_head keys all-gathered,
+    argmax and accept length per sequence, each sequence against the oracle."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    import iam_b200 as I
+    from gpu_util import cosine, rel_err
+    from test_gpu_engine import cdims, check_argmax
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        d, ctx, n, K = O.TINY, 6, 3, 4
+        W = SM.make_weights(SEED, d)
+        tokens = np.stack([SM.draft_tokens(SEED, d, K, tag=f"tpb{q}") for q in range(n)])
+        pos = np.array([ctx, ctx + 2, ctx + 5], np.int32)
+        obj = [I.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        dims = cdims(d, ctx + 32, n * K)
+        dims.max_seqs = n
+        e = I.Engine(dims, device=rank, rank=rank, world=world, nccl_id=obj[0])
+        try:
+            e.init_synthetic(SEED)
+            e.state_init(SEED, ctx)
+            dist.barrier()
+            am, acc = e.verify_batch(tokens, pos)
+            hid = O.from_u16(e.read_hidden(n * K)).reshape(n, K, d.hidden)
+            for q in range(n):
+                st = SM.make_state(SEED, d, ctx, ctx + 32, slot=q)
+                am_r, acc_r, normed, logits = O.model_step(tokens[q], int(pos[q]), W, st, d, return_hidden=True)
+                check_argmax(am[q], logits)
+                assert rel_err(hid[q], normed) <= 1e-2 and cosine(hid[q], normed) >= 0.9999, q
+                if np.array_equal(am[q], am_r):
+                    assert acc[q] == acc_r
+            dist.barrier()
+        finally:
+            e.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_batch_matches_oracle():
+    import torch.multiprocessing as mp
+
+    mp.spawn(_rank_batch, args=(2, _free_port()), nprocs=2, join=True)
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_tp2_verify_matches_oracle():
     import torch.multiprocessing as mp
