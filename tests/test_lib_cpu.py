@@ -40,3 +40,15 @@ def test_dims_defaults_are_qwen35_27b():
     assert (d.hidden, d.intermediate, d.vocab, d.n_layers) == (5120, 17408, 248320, 64)
     assert (d.gdn_k_heads, d.gdn_v_heads, d.n_heads, d.n_kv_heads, d.head_dim) == (16, 48, 24, 4, 256)
     assert abs(d.rope_theta - 1e7) < 1 and d.rotary_dim == 64
+    assert d.max_seqs == 1
+
+
+def test_sequence_slots_are_validated():
+    """max_seqs (the multi-sequence verify's slots) must lie in 1..max_rows;
+    checked by the host-only shard planner, no GPU involved."""
+    for bad in (0, 129):
+        d = I.Dims.qwen35_27b(max_rows=128, max_seqs=bad)
+        with pytest.raises(I.IamError) as err:
+            I.tp_shard_of(d, 0, 1)
+        assert err.value.status == I.IAM_EINVAL and "max_seqs" in str(err.value)
+    I.tp_shard_of(I.Dims.qwen35_27b(max_rows=512, max_seqs=64), 0, 8)
