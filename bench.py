@@ -248,8 +248,8 @@ def run_gpu(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "kernel": "qmm_tc_kernel", "achieved": q_gbs, "peak": hbm, "unit": "GB/s",
                      "frac": q_gbs / hbm,
                      "traffic": TRAFFIC_PER_WEIGHT_BYTE * q["bytes"] / max(q["launches"], 1),
-                     "traffic_note": "DRAM read+write per average launch, scaled from the ncu capture in "
-                                     "profiles/qmm_tc_34816x5120_m32.md by weight bytes",
+                     "traffic_note": "DRAM read+write per average launch: the weight bytes times the "
+                                     "traffic / weight-bytes ratio of one ncu capture (34816 x 5120, 32 tokens)",
                      "peak_kind": peak_kind, "launches_per_step": q["launches"], "ms_per_step": q["ms"],
                      "timing": "eager step, CUDA events on the engine stream around each launch"},
         "kernels_ms": {k: round(v["ms"], 4) for k, v in prof.items()},

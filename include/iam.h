@@ -54,6 +54,9 @@ int iam_version(void);
  * w: uint32 [N, K/8], nibble i of word j = column 8j+i (low nibble first);
  * s, b: bf16 [N, K/64]; x: bf16 [M, K]; y: bf16 [M, N].
  * Requires K % 64 == 0, N % 8 == 0, 1 <= M.
+ * Split-K scratch: one library workspace per (device, stream), grown on
+ * demand; calls on one stream are ordered, calls on different streams never
+ * share a workspace.  The same holds for iam_qmm_affine4_packed.
  * Replaces dispatchQMatmul (full_forward.swift:711-728) / encodeQMM
  * (batch_verify_27b.swift:100-119), which bind MLX's
  * affine_qmm_t_nax_bfloat16_t_gs_64_b_4 kernel with args (w,s,b,x,y,K,N,M). */
@@ -66,13 +69,21 @@ int iam_qmm_affine4(const uint32_t* w, const uint16_t* s, const uint16_t* b, con
  * reference.  Same arguments, kernel and results; the split-K scratch is a
  * fixed array inside the library (1 Mi floats, 16 Ki counters) instead of a
  * workspace grown on demand, and a shape whose plan needs more is rejected
- * with IAM_EINVAL.  The first call on a device looks the scratch up
- * (cudaGetSymbolAddress) and clears it (cudaMemset, synchronous); make it
- * outside any stream capture.  The scratch is
+ * with IAM_EINVAL (iam_qmm_affine4_plan tells a caller in advance).  Every
+ * call looks the scratch's device address up (cudaGetSymbolAddress); the
+ * first call on a device also clears it with cudaMemsetAsync on the call's
+ * stream, so make that first call outside any stream capture.  The scratch is
  * shared by all calls on a device: calls must not overlap (one stream, or
  * ordered), and a call that failed part-way may leave it dirty. */
 int iam_qmm_affine4_noalloc(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
                             uint16_t* y, int M, int N, int K, int group_size, void* stream);
+
+/* The plan iam_qmm_affine4 and iam_qmm_affine4_noalloc run for an [M, K] x
+ * [N, K]^T shape on the current device: the largest number of CTAs that
+ * split K in one pass (1: no split-K scratch is used), and the split-K
+ * scratch it needs (floats, counters; 0 when nothing is split).  No
+ * counterpart in the reference. */
+int iam_qmm_affine4_plan(int M, int N, int K, int* splits, size_t* scratch_floats, size_t* scratch_counters);
 
 /* The same matmul on the tensor cores (tcgen05, bf16 weights dequantized into
  * tensor memory) over weights re-packed once into 128-row x 256-k blocks.

@@ -26,6 +26,9 @@
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <functional>
+#include <map>
+#include <mutex>
 
 #include "kernels.cuh"
 #include "tma.cuh"
@@ -814,34 +817,47 @@ size_t qmm_ws_counters(const QmmArgs& a, const QmmConfig& c) {
 
 namespace {
 // Split-K workspace of the operator-level entry points: library-owned, zeroed,
-// grown on demand, one per device.  (The engine passes its own.)
+// grown on demand, one per (device, stream, kind), so calls on different
+// streams never share one.  (The engine passes its own.)
 struct OpWs {
   float* ws = nullptr;
   int* ctr = nullptr;
   size_t floats = 0, ctrs = 0;
 };
-// [device][kind]: the mma.sync kernels sum partials into a workspace they keep
-// zeroed; the tensor-core kernel stores partials without clearing them, so the
-// two never share one.
-OpWs g_opws[64][2];
+// kind: the mma.sync kernels sum partials into a workspace they keep zeroed;
+// the tensor-core kernel stores partials without clearing them, so the two
+// never share one.
+struct OpWsKey {
+  int dev;
+  cudaStream_t st;
+  int kind;
+  bool operator<(const OpWsKey& o) const {
+    if (dev != o.dev) return dev < o.dev;
+    if (st != o.st) return std::less<cudaStream_t>()(st, o.st);
+    return kind < o.kind;
+  }
+};
+std::mutex g_opws_mu;
+std::map<OpWsKey, OpWs> g_opws;
 
 }  // namespace
 
 int qmm_op_workspace(int kind, size_t floats, size_t ctrs, cudaStream_t st, float** ws, int** ctr) {
   int dev = 0;
   IAM_CUDA(cudaGetDevice(&dev));
-  IAM_CHECK(dev >= 0 && dev < 64, "qmm: device index out of range");
   IAM_CHECK(kind == 0 || kind == 1, "qmm: workspace kind");
-  OpWs& w = g_opws[dev][kind];
+  std::lock_guard<std::mutex> lock(g_opws_mu);
+  OpWs& w = g_opws[OpWsKey{dev, st, kind}];
   if (w.floats < floats || w.ctrs < ctrs) {
+    // the stream's earlier calls may still read the old workspace
     IAM_CUDA(cudaStreamSynchronize(st));
     cudaFree(w.ws);
     cudaFree(w.ctr);
     w = OpWs{};
     IAM_CUDA(cudaMalloc(&w.ws, floats * sizeof(float)));
     IAM_CUDA(cudaMalloc(&w.ctr, ctrs * sizeof(int)));
-    IAM_CUDA(cudaMemset(w.ws, 0, floats * sizeof(float)));
-    IAM_CUDA(cudaMemset(w.ctr, 0, ctrs * sizeof(int)));
+    IAM_CUDA(cudaMemsetAsync(w.ws, 0, floats * sizeof(float), st));
+    IAM_CUDA(cudaMemsetAsync(w.ctr, 0, ctrs * sizeof(int), st));
     w.floats = floats;
     w.ctrs = ctrs;
   }
@@ -954,16 +970,14 @@ namespace iam {
 namespace {
 constexpr size_t kNoAllocFloats = static_cast<size_t>(1) << 20;  // 4 MiB of fp32 partial sums
 constexpr size_t kNoAllocCounters = 16384;                        // one arrival counter a row block
-// Both must be zero when a call starts: the first call on a device clears them
-// and every call that completes leaves them zero again (the last CTA of a row
-// block clears what it summed).
+// Both must be zero when a call starts.  They are zero when the module loads
+// (static storage), the first call on a device clears them again, ordered on
+// the caller's stream, and every call that completes leaves them zero (the
+// last CTA of a row block clears what it summed).
 __device__ __align__(256) float g_noalloc_ws[kNoAllocFloats];
 __device__ __align__(256) int g_noalloc_ctr[kNoAllocCounters];
-struct NoAllocScratch {
-  float* ws = nullptr;
-  int* ctr = nullptr;
-};
-NoAllocScratch g_noalloc[64];  // device addresses, looked up once per device
+std::mutex g_noalloc_mu;
+bool g_noalloc_cleared[64] = {};  // per device: the first call's clear was enqueued
 }  // namespace
 }  // namespace iam
 
@@ -977,16 +991,20 @@ extern "C" int iam_qmm_affine4_noalloc(const uint32_t* w, const uint16_t* s, con
   int dev = 0;
   IAM_CUDA(cudaGetDevice(&dev));
   IAM_CHECK(dev >= 0 && dev < 64, "iam_qmm_affine4_noalloc: device index out of range");
-  NoAllocScratch& sc = g_noalloc[dev];
-  if (!sc.ws) {  // first call on this device: a lookup and a clear, no allocation
-    float* ws = nullptr;
-    int* ctr = nullptr;
-    IAM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&ws), g_noalloc_ws));
-    IAM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&ctr), g_noalloc_ctr));
-    IAM_CUDA(cudaMemset(ws, 0, kNoAllocFloats * sizeof(float)));
-    IAM_CUDA(cudaMemset(ctr, 0, kNoAllocCounters * sizeof(int)));
-    sc.ws = ws;
-    sc.ctr = ctr;
+  const cudaStream_t st = as_stream(stream);
+  // The arrays' device addresses, looked up on every call: a host-side
+  // lookup, and never stale after the device's context was re-created.
+  float* ws = nullptr;
+  int* ctr = nullptr;
+  IAM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&ws), g_noalloc_ws));
+  IAM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&ctr), g_noalloc_ctr));
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_cleared[dev]) {  // first call on this device: a stream-ordered clear, no allocation
+      IAM_CUDA(cudaMemsetAsync(ws, 0, kNoAllocFloats * sizeof(float), st));
+      IAM_CUDA(cudaMemsetAsync(ctr, 0, kNoAllocCounters * sizeof(int), st));
+      g_noalloc_cleared[dev] = true;
+    }
   }
   QmmArgs a = {};
   a.x = x;
@@ -1014,7 +1032,35 @@ extern "C" int iam_qmm_affine4_noalloc(const uint32_t* w, const uint16_t* s, con
                                   std::to_string(nc) + " counters of split-K scratch; the fixed scratch holds " +
                                   std::to_string(kNoAllocFloats) + " and " + std::to_string(kNoAllocCounters));
   }
-  a.ws = sc.ws;
-  a.counters = sc.ctr;
-  return qmm_run(a, as_stream(stream), false, kNoAllocFloats, kNoAllocCounters);
+  a.ws = ws;
+  a.counters = ctr;
+  return qmm_run(a, st, false, kNoAllocFloats, kNoAllocCounters);
+}
+
+extern "C" int iam_qmm_affine4_plan(int M, int N, int K, int* splits, size_t* scratch_floats,
+                                    size_t* scratch_counters) {
+  using namespace iam;
+  IAM_CHECK(N > 0 && N % 8 == 0 && M >= 1 && K > 0 && K % 64 == 0, "iam_qmm_affine4_plan: bad shape");
+  IAM_CHECK(splits && scratch_floats && scratch_counters, "iam_qmm_affine4_plan: null output");
+  QmmArgs a = {};
+  a.ldx = K;
+  a.K = K;
+  a.nseg = 1;
+  a.seg[0].rows = N;
+  a.seg[0].mode = EPI_STORE;
+  *splits = 1;
+  *scratch_floats = 0;
+  *scratch_counters = 0;
+  // passes of 32 tokens and a remainder, as iam_qmm_affine4 runs them
+  for (int pm : {std::min(M, 32), M % 32}) {
+    if (pm == 0) continue;
+    QmmArgs probe = a;
+    probe.M = pm;
+    const QmmConfig c = qmm_plan(probe);
+    *splits = std::max(*splits, c.ks);
+    if (c.ks < 2) continue;
+    *scratch_floats = std::max(*scratch_floats, qmm_ws_floats(probe, c));
+    *scratch_counters = std::max(*scratch_counters, qmm_ws_counters(probe, c));
+  }
+  return IAM_OK;
 }

@@ -28,6 +28,7 @@ _SIGS = {
     "iam_version": (_i, []),
     "iam_qmm_affine4": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "iam_qmm_affine4_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "iam_qmm_affine4_plan": (_i, [_i, _i, _i, C.POINTER(C.c_int), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "iam_qmm_packed_bytes": (_sz, [_i, _i]),
     "iam_qmm_pack_affine4": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "iam_qmm_affine4_packed": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
@@ -121,6 +122,13 @@ def qmm_affine4(w, s, b, x, y, M, N, K, group_size=64, stream=None):
 
 def qmm_affine4_noalloc(w, s, b, x, y, M, N, K, group_size=64, stream=None):
     _check(lib().iam_qmm_affine4_noalloc(w, s, b, x, y, M, N, K, group_size, _s(stream)))
+
+
+def qmm_affine4_plan(M, N, K):
+    """(splits, scratch floats, scratch counters) of the matmul plan for a shape."""
+    ks, nf, nc = C.c_int(0), C.c_size_t(0), C.c_size_t(0)
+    _check(lib().iam_qmm_affine4_plan(M, N, K, C.byref(ks), C.byref(nf), C.byref(nc)))
+    return ks.value, nf.value, nc.value
 
 
 def qmm_packed_bytes(N, K) -> int:

@@ -114,9 +114,24 @@ def unpack_codes(w: np.ndarray) -> np.ndarray:
 EXACT_DEQUANT = False
 
 
+# An implementation computing the same bits faster (oracle/fast.py, checked
+# against this function by tests/test_oracle_fast.py), or None.
+_DEQUANT_IMPL = None
+
+
+def set_dequant_impl(fn):
+    """Routes dequant() through ``fn`` (None: this module's numpy statement);
+    returns the previous setting."""
+    global _DEQUANT_IMPL
+    prev, _DEQUANT_IMPL = _DEQUANT_IMPL, fn
+    return prev
+
+
 def dequant(w, s, b, group: int = 64) -> np.ndarray:
     """MLX affine dequant to bf16: w = bf16(q * scale + bias), computed in fp32
     (float(nibble) * scale + bias, full_forward.swift:129-132)."""
+    if _DEQUANT_IMPL is not None and not EXACT_DEQUANT:
+        return _DEQUANT_IMPL(w, s, b, group)
     q = unpack_codes(w).astype(np.float32)
     sc = np.repeat(np.asarray(s, np.float32), group, axis=-1)
     bi = np.repeat(np.asarray(b, np.float32), group, axis=-1)

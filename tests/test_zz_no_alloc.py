@@ -21,6 +21,8 @@ import iam_b200 as I  # noqa: E402
 
 @pytest.mark.parametrize("N,K,M", [(1024, 5120, 8), (5120, 17408, 4), (48, 5120, 40)])
 def test_noalloc_matches_qmm_affine4_twice(N, K, M):
+    ks, nf, nc = I.qmm_affine4_plan(M, N, K)
+    assert ks > 1 and 0 < nf <= 1 << 20 and 0 < nc <= 16384, (ks, nf, nc)  # the fixed scratch is in use
     w, s, b = synth.gen_qweight(71, f"t.noalloc.{N}x{K}", N, K)
     x = synth.gen_normal_bf16(72, f"t.noalloc.x.{M}x{K}", M * K, 1.0).reshape(M, K)
     keep = [dev(w, torch), dev(s.view(np.uint16), torch), dev(b.view(np.uint16), torch), dev(x.view(np.uint16), torch)]
@@ -37,6 +39,22 @@ def test_noalloc_matches_qmm_affine4_twice(N, K, M):
         assert_close_bf16(got, O.from_u16(want).astype(np.float32), rel=1e-3, cos=0.999999)
         assert np.mean(got != want) < 0.01
         assert_close_bf16(got, oracle)
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch():
+    """A plan whose split-K scratch exceeds the fixed array is an IAM_EINVAL,
+    reported before anything is launched (the pointers are never read)."""
+    big = None
+    for N, K, M in ((4096, 65536, 32), (8192, 131072, 32), (16384, 131072, 32)):
+        ks, nf, nc = I.qmm_affine4_plan(M, N, K)
+        if nf > 1 << 20 or nc > 16384:
+            big = (N, K, M)
+            break
+    assert big is not None, "no candidate shape exceeds the fixed scratch"
+    N, K, M = big
+    with pytest.raises(I.IamError) as err:
+        I.qmm_affine4_noalloc(16, 16, 16, 16, 16, M, N, K)
+    assert err.value.status == I.IAM_EINVAL
 
 
 def test_noalloc_rejects_bad_arguments():
