@@ -5,8 +5,9 @@ MLX affine 4-bit weights, bf16 embedding, 4-bit lm_head), random-init
 synthetic weights generated on the GPU, seeded recurrent state and a KV cache
 of 1024 prior tokens; each step verifies K = 32 draft tokens (the headline)
 and, reported alongside, K = 1 (plain decode).  One step = one pass of the
-whole stack over the K tokens + lm_head argmax + accept length; positions
-advance by K every step (context 1024 -> 1024 + (W+S)*K).
+whole stack over the K tokens + lm_head argmax + accept length at positions
+1024..1024+K-1: every step re-verifies its block at context 1024 (the
+recurrent state carries on from step to step).
 
   python bench.py [--gpus N] [--steps S] [--warmup W] [--k 32] [--impl reference]
   python bench.py --batch 64 --k 8 [--ctx 4096]   # multi-sequence verify (one line, token-rows/s)
@@ -38,6 +39,12 @@ TRAFFIC_PER_WEIGHT_BYTE = 104.090624 / 100.270080
 WORKLOAD = "qwen3.5-27b-shape 64-layer (48 GDN + 16 attn) 4-bit verify, ctx 1024, batch 1"
 
 
+def bench_config(K: int, world: int) -> dict:
+    """The workload, shared by both arms' lines."""
+    return {"workload": WORKLOAD, "K": K, "ctx": CTX, "batch": 1, "parallelism": f"tp{world}",
+            "l2": "inputs larger than L2 (14.4 GB of weights streamed per step)"}
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -49,86 +56,128 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """One ``nvidia-smi --query-gpu=... -lms 50`` process, started before the
+    warm-up (so no process start falls inside the timed region) and stopped
+    after it; the samples whose timestamps lie in the timed window [begin(),
+    end()] are summarised."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu: int):
         self.gpu = gpu
-        self.samples = []
-        self._stop = threading.Event()
-        self._t = None
+        self.proc = None
+        self.t0 = self.t1 = None
 
     def start(self):
-        def run():
-            while not self._stop.is_set():
-                try:
-                    out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                         timeout=5).stdout.strip()
-                    if out:
-                        self.samples.append([x.strip() for x in out.split(",")])
-                except Exception:
-                    pass
-                self._stop.wait(0.2)
-        self._t = threading.Thread(target=run, daemon=True)
-        self._t.start()
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)  # the first sample is out before any timing starts
+
+    def begin(self):
+        import datetime
+        self.t0 = datetime.datetime.now()
+
+    def end(self):
+        import datetime
+        self.t1 = datetime.datetime.now()
 
     def stop(self):
-        self._stop.set()
-        if self._t:
-            self._t.join(timeout=10)
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        import datetime
+        rows = []
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=10)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            for line in out.splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 10:
+                    continue
+                try:
+                    ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f")
+                except ValueError:
+                    continue
+                rows.append((ts, f[1:]))
+        inside = [r for ts, r in rows if self.t0 and self.t1 and self.t0 <= ts <= self.t1]
+        if not inside and rows and self.t0:
+            # a window shorter than the sampling period: the samples either side of it
+            before = [r for ts, r in rows if ts <= self.t0][-1:]
+            after = [r for ts, r in rows if self.t1 and ts >= self.t1][:1]
+            inside = before + after
+        sm = [float(r[1]) for r in inside if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in inside if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+        reasons = sorted({names[i] for r in inside for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+                "reasons": reasons, "samples": len(inside), "sampling": "nvidia-smi -lms 50, timed window"}
 
 
 # ---------------------------------------------------------------- CPU legs (oracle)
 def oracle_sample(K: int, threads: int):
-    """Time the CPU restatement (numpy fp32, dequant included) on one GDN layer,
-    one attention layer and 1/16 of the lm_head at full size; extrapolate to
-    the 64-layer step.  Returns (tokens/s, seconds of CPU work, description)."""
+    """Time the CPU restatement (numpy fp32 with the multi-threaded C dequant
+    helper, dequantisation included) on a bounded sample of the step at full
+    size: one GDN layer, one attention layer and 1/16 of the lm_head.  Returns
+    (tokens/s of the 64-layer step extrapolated x48/x16/x16, seconds the sample
+    took, description)."""
     import numpy as np
+    from oracle import fast as F
     from oracle import iam_oracle as O
     from oracle import synth_model as SM
     d = O.QWEN35_27B
-    W = SM.make_layer(SEED, d, 0)
-    W.update(SM.make_layer(SEED, d, 3))
+    W = F.make_layer(SEED, d, 0)
+    W.update(F.make_layer(SEED, d, 3))
     st = SM.make_state(SEED, d, CTX, CTX + K, layers=[0, 3])
     lm_rows = d.vocab // 16
-    w, s, b = SM.make_tensor(SEED, "lm_head", "q4", (lm_rows, d.hidden), None)
+    lm = F.gen_qweight(SEED, "lm_head", lm_rows, d.hidden)
     x = SM.hidden_input(SEED, d, K)
-    t0 = time.perf_counter()
-    O.gdn_block(x, W, "model.layers.0.", st.conv[0], st.S[0], d)
-    t1 = time.perf_counter()
-    O.attn_block(x, W, "model.layers.3.", st.k_cache[3], st.v_cache[3], CTX, d)
-    t2 = time.perf_counter()
-    O.argmax_first(O.qmm_affine4(O.rms_norm(x, np.ones(d.hidden, np.float32)), w, s, b))
-    t3 = time.perf_counter()
+    with F.fast_dequant():
+        t0 = time.perf_counter()
+        O.gdn_block(x, W, "model.layers.0.", st.conv[0], st.S[0], d)
+        t1 = time.perf_counter()
+        O.attn_block(x, W, "model.layers.3.", st.k_cache[3], st.v_cache[3], CTX, d)
+        t2 = time.perf_counter()
+        O.argmax_first(O.qmm_affine4(O.rms_norm(x, np.ones(d.hidden, np.float32)), *lm))
+        t3 = time.perf_counter()
     step = 48 * (t1 - t0) + 16 * (t2 - t1) + 16 * (t3 - t2)
-    desc = (f"numpy fp32 oracle, {threads} threads: 1 GDN layer {t1 - t0:.2f}s + 1 attention layer {t2 - t1:.2f}s "
-            f"+ 1/16 lm_head {t3 - t2:.2f}s at K={K}, ctx {CTX}, extrapolated x48/x16/x16 to the 64-layer step")
+    desc = (f"numpy fp32 oracle + C dequant, {threads} threads: 1 GDN layer {t1 - t0:.2f}s + 1 attention layer "
+            f"{t2 - t1:.2f}s + 1/16 lm_head {t3 - t2:.2f}s at K={K}, ctx {CTX}, extrapolated x48/x16/x16 to "
+            f"the 64-layer step")
     return K / step, t3 - t0, desc
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the CPU restatement of the path (the reference's own
+    implementation is Swift + Metal + a binary MLX kernel and cannot run here).
+    Each step is one bounded sample (oracle_sample); the line reports the
+    sample's measured time per step and the 64-layer step time extrapolated
+    from it, marked as extrapolated."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    vals = []
+    vals, secs = [], []
+    desc = ""
     for i in range(args.warmup + args.steps):
-        v, _, desc = oracle_sample(args.k, threads)
+        v, sec, desc = oracle_sample(args.k, threads)
         if i >= args.warmup:
             vals.append(v)
+            secs.append(sec)
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * args.k / value,
+        "extrapolated": True,
+        "sample_ms_per_step": 1000.0 * statistics.median(secs),
+        "sample_pieces": ["1 GDN layer x48", "1 attention layer x16", "1/16 of the lm_head x16"],
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "K": args.k, "ctx": CTX, "parallelism": "cpu"},
+        "config": bench_config(args.k, world),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -167,21 +216,24 @@ def run_gpu(args, rank, world, local_rank):
         torch.cuda.synchronize()
 
     def device_run(kk: int):
+        clk = ClockSampler(local_rank)
+        clk.start()
         eng.state_init(SEED, CTX)
         toks = torch.from_numpy(rng.integers(0, dims.vocab, kk).astype(np.int32)).cuda()
         out = torch.zeros(kk, dtype=torch.int32, device="cuda")
-        eng.verify_device(toks.data_ptr(), kk, CTX, out.data_ptr(), sh)
-        for _ in range(args.warmup - 1):
-            eng.verify_device(toks.data_ptr(), kk, -1, out.data_ptr(), sh)
+        # every step verifies the block at positions CTX..CTX+kk-1 (the KV rows
+        # of the block are rewritten each step), so each runs at context CTX
+        for _ in range(args.warmup):
+            eng.verify_device(toks.data_ptr(), kk, CTX, out.data_ptr(), sh)
         barrier()
-        clk = ClockSampler(local_rank)
-        clk.start()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk.begin()
         a.record(stream)
         for _ in range(args.steps):
-            eng.verify_device(toks.data_ptr(), kk, -1, out.data_ptr(), sh)
+            eng.verify_device(toks.data_ptr(), kk, CTX, out.data_ptr(), sh)
         b.record(stream)
         torch.cuda.synchronize()
+        clk.end()
         ms = a.elapsed_time(b) / args.steps
         clocks = clk.stop()
         if dist is not None:
@@ -197,15 +249,12 @@ def run_gpu(args, rank, world, local_rank):
     # end to end through the public C API: host tokens in, host argmax out
     eng.state_init(SEED, CTX)
     htoks = rng.integers(0, dims.vocab, K).astype(np.int32)
-    pos = CTX
     for _ in range(args.warmup):
-        eng.verify(htoks, pos)
-        pos += K
+        eng.verify(htoks, CTX)
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        eng.verify(htoks, pos)
-        pos += K
+        eng.verify(htoks, CTX)
     e2e_s = (time.perf_counter() - t0) / args.steps
     if dist is not None:
         t = torch.tensor([e2e_s], device="cuda")
@@ -240,8 +289,7 @@ def run_gpu(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "K": K, "ctx": CTX, "batch": 1, "parallelism": f"tp{world}",
-                   "l2": "inputs larger than L2 (14.4 GB of weights streamed per step)"},
+        "config": bench_config(K, world),
         "k1": {"value": 1000.0 / ms1, "unit": "tokens/s", "ms_per_step": ms1},
         "hbm_roofline_step": {"bytes_per_step_per_gpu": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": hbm,
                               "frac": step_gbs / hbm, "peak_kind": peak_kind},
@@ -324,18 +372,20 @@ def run_batch(args, rank, world, local_rank):
     toks = torch.from_numpy(htoks.reshape(-1)).cuda()
     pos0 = torch.full((n,), ctx, dtype=torch.int32, device="cuda")
     out = torch.zeros(n * K, dtype=torch.int32, device="cuda")
+    clk = ClockSampler(local_rank)
+    clk.start()
     eng.verify_batch_device(toks.data_ptr(), n, K, pos0.data_ptr(), out.data_ptr(), None, sh)
     for _ in range(args.warmup - 1):
         eng.verify_batch_device(toks.data_ptr(), n, K, None, out.data_ptr(), None, sh)
     barrier()
-    clk = ClockSampler(local_rank)
-    clk.start()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk.begin()
     a.record(stream)
     for _ in range(args.steps):
         eng.verify_batch_device(toks.data_ptr(), n, K, None, out.data_ptr(), None, sh)
     b.record(stream)
     torch.cuda.synchronize()
+    clk.end()
     ms = a.elapsed_time(b) / args.steps
     clocks = clk.stop()
     if dist is not None:
