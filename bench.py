@@ -528,6 +528,60 @@ def _profile_one_qmm(spec):
     print(json.dumps({"profile_qmm": [N, K, M], "kernel": "mma.sync" if mlx else "tcgen05"}))
 
 
+def qmm_sweep(args):
+    """Warm per-launch time of the W4A16 matmul on packed weights, per shape
+    and token count, on the GEMV kernel (the library's choice up to 16
+    tokens) and on the tensor-core kernel: one JSON line each.  Enough copies
+    of each matrix are cycled that every launch streams its weights from HBM
+    (more than the 126 MB L2 between two uses of a copy); CUDA events on the
+    launching stream around --steps launches after --warmup."""
+    import torch
+    import iam_b200 as I
+    ms = [int(v) for v in args.qmm_ms.split(",")]
+    hbm, kind = peaks()
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    for spec in args.qmm_sweep.split(";"):
+        N, K = (int(v) for v in spec.split(","))
+        g = torch.Generator(device="cuda").manual_seed(0)
+        w = torch.randint(-2**31, 2**31 - 1, (N, K // 8), dtype=torch.int32, device="cuda", generator=g)
+        sc = (torch.rand(N, K // 64, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        b = (-8 * sc.float()).to(torch.bfloat16)
+        nb = I.qmm_packed_bytes(N, K)
+        copies = max(2, -(-300_000_000 // nb))
+        pk = [torch.empty(nb, dtype=torch.uint8, device="cuda") for _ in range(copies)]
+        for p_ in pk:
+            I.qmm_pack_affine4(w.data_ptr(), sc.data_ptr(), b.data_ptr(), p_.data_ptr(), N, K, st.cuda_stream)
+        del w
+        wbytes = N * K * (0.5 + 4 / 64)
+        for M in ms:
+            x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+            y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            for kern in ("gemv", "tcgen05"):
+                if kern == "gemv" and M > 16:
+                    continue
+                os.environ["IAM_QMM_GEMV_MAX_M"] = "16" if kern == "gemv" else "0"
+                n = args.warmup + args.steps
+                for i in range(args.warmup):
+                    I.qmm_affine4_packed(pk[i % copies].data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K,
+                                         st.cuda_stream)
+                a, bb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(st)
+                for i in range(args.warmup, n):
+                    I.qmm_affine4_packed(pk[i % copies].data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K,
+                                         st.cuda_stream)
+                bb.record(st)
+                torch.cuda.synchronize()
+                us = a.elapsed_time(bb) * 1000.0 / args.steps
+                print(json.dumps({"qmm_sweep": [N, K, M], "kernel": kern, "us": round(us, 2),
+                                  "gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+                                  "hbm_frac": round(wbytes / (us * 1e-6) / 1e9 / hbm, 4), "peak_kind": kind}),
+                      flush=True)
+        os.environ.pop("IAM_QMM_GEMV_MAX_M", None)
+        del pk
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -540,11 +594,15 @@ def main():
     ap.add_argument("--profile-qmm", default=None,
                     help="N,K,M[,mlx];...: a few launches of each matmul (tensor-core, or mma.sync on the MLX layout), for ncu")
     ap.add_argument("--sweep", default=None, help="K1,K2,...: step time per verify width on one GPU")
+    ap.add_argument("--qmm-sweep", default=None, help="N,K;...: warm matmul time per shape, token count and kernel")
+    ap.add_argument("--qmm-ms", default="1,2,4,8,16,32", help="token counts of --qmm-sweep")
     ap.add_argument("--batch", type=int, default=0, help="sequences of a multi-sequence verify step (with --k)")
     ap.add_argument("--ctx", type=int, default=4096, help="prior KV tokens per sequence of --batch")
     args = ap.parse_args()
     if args.sweep:
         return sweep(args)
+    if args.qmm_sweep:
+        return qmm_sweep(args)
     if args.profile_step:
         return profile_step(args)
     if args.profile_qmm:

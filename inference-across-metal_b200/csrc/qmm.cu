@@ -891,7 +891,10 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
         if (s.resid) s.resid += static_cast<size_t>(m0) * s.ldr;
         if (s.keys) s.keys += m0;
       }
-      const int r = qmm_tc_run(p, st, pdl, ws_floats_cap, ws_ctr_cap);
+      // narrow passes convert the weights in registers (mma.sync); wider ones
+      // on the tensor cores
+      const int r = p.M <= qmm_gemv_max_m() ? qmm_gemv_run(p, st, pdl, ws_floats_cap, ws_ctr_cap)
+                                            : qmm_tc_run(p, st, pdl, ws_floats_cap, ws_ctr_cap);
       if (r != IAM_OK) return r;
     }
     return IAM_OK;

@@ -85,24 +85,43 @@ inline int qmm_rows_per_cta(int mode, int rt) { return (mode == EPI_SWIGLU ? 8 :
 QmmConfig qmm_plan(QmmArgs& a);
 int qmm_launch(const QmmArgs& a, const QmmConfig& c, cudaStream_t st, bool pdl);
 
-// ---- tile-packed weights for the tensor-core kernel (qmm_tc.cu)
+// ---- tile-packed weights for the tensor-core and GEMV kernels (qmm_tc.cu,
+// qmm_gemv.cu)
 //
 // A matrix of `rows` x K becomes ceil(rows / 128) tiles (SwiGLU pairs: 64
 // features a tile, gate rows 0-63 and up rows 64-127) of ceil(K / 256)
 // blocks of kQpBlockBytes, tile-major:
 //   block (t, kb) at (t * KB + kb) * kQpBlockBytes;
-//   codes: row r at r * 128, its 32-k chunk c (4 words) at ((c ^ (r & 7)) * 16);
+//   codes: row r at r * 128, its 32-k chunk c (4 words) at ((c ^ qp_swz(r)) * 16);
 //     each word holds 8 consecutive k with nibble s = k 2s, nibble s+4 = k 2s+1
 //     (so (w >> 4s) & 0x000F000F is the natural pair (k 2s, k 2s+1));
 //   (scale, bias) of row r, group g (0..3) at kQpCodeBytes + r * 16 + g * 4
 //     (scale in the low half);
-// then one byte a tile: 1 when every scale of the tile is below 0.25 in
-// magnitude, in which case the tile's scales are stored multiplied by 2^130
+// then one byte a tile: 1 when every scale of the tile is below 0.5 in
+// magnitude, in which case the tile's scales are stored multiplied by 2^129
 // (exact: a power of two, and the product stays below the bf16 maximum).
-// Such tiles are converted with the code as a bf16 subnormal q * 2^-130 and
-// one packed FMA, fma(q * 2^-130, s * 2^130, b) = bf16(q * s + b) with one
-// rounding -- the same bits as the general form, one instruction fewer a pair.
+// Such tiles are converted with the code in bits 4-7 of each 16-bit half: as
+// a bf16 bit pattern that is q * 2^-129 (subnormal for q < 8, the smallest
+// normal binade for q >= 8 -- one linear scale across both), so one packed
+// FMA, fma(q * 2^-129, s * 2^129, b) = bf16(q * s + b) with the product exact
+// and one rounding -- the same bits as the general form in fewer instructions.
 // Padding rows and k read as zero codes with zero scale and bias.
+//
+// The chunk swizzle qp_swz(r) is a bijection of r % 8 that keeps both readers
+// free of shared-memory bank conflicts: the tensor-core kernel's 16-byte
+// loads of one chunk by 8 consecutive rows, and the GEMV kernel's 8-byte
+// loads of word pairs by 4 consecutive rows x 4 lanes.
+__host__ __device__ __forceinline__ int qp_swz(int r) { return ((r & 3) << 1) | ((r >> 2) & 1); }
+
+// The four code pairs of a packed word in bits 4-7 of each half (the fast
+// conversion's operand): pair s = (k 2s, k 2s+1) in v[s].
+__device__ __forceinline__ void qp_codes_hi(uint32_t w, uint32_t (&v)[4]) {
+  v[0] = (w << 4) & 0x00F000F0u;
+  v[1] = w & 0x00F000F0u;
+  v[2] = (w >> 4) & 0x00F000F0u;
+  v[3] = (w >> 8) & 0x00F000F0u;
+}
+
 constexpr int kQpRows = 128;
 constexpr int kQpBlockK = 256;
 constexpr int kQpCodeBytes = kQpRows * kQpBlockK / 2;   // 16384
@@ -116,7 +135,7 @@ inline int qp_tiles(int rows, bool swiglu) { return (rows + (swiglu ? 63 : 127))
 
 // Packing, in three stream-ordered steps per packed matrix `dst` of `tiles`
 // tiles: qmm_pack_begin sets every tile flag; qmm_pack_scan clears the flag
-// of each tile holding a scale >= 0.25 in magnitude (or not finite) among
+// of each tile holding a scale >= 0.5 in magnitude (or not finite) among
 // the rows of one source; qmm_pack then writes the rows of one source.  A
 // source's row r goes to tile r / per_tile, tile row row_off + r % per_tile
 // (per_tile 128 with row_off 0, or 64 with row_off 0 / 64 for the gate / up
@@ -126,9 +145,16 @@ int qmm_pack_scan(const uint16_t* s, int rows, int K, unsigned char* dst, int ti
 int qmm_pack(const uint32_t* w, const uint16_t* s, const uint16_t* b, int rows, int K, unsigned char* dst,
              int tiles, int per_tile, int row_off, cudaStream_t st);
 
-// Tensor-core matmul over packed segments (every segment has `packed`; M <= 32).
+// Tensor-core matmul over packed segments (every segment has `packed`; M <= 64).
 // A null a.ws selects the library's own split-K workspace.
 int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap);
+// Register-dequant matmul over packed segments for narrow passes (M <= 16):
+// mma.sync on weights converted in registers, no tensor memory.
+constexpr int kGemvMaxM = 16;
+int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap);
+// Widest pass that qmm_run sends to the GEMV kernel (IAM_QMM_GEMV_MAX_M
+// overrides: 0 sends every pass to the tensor-core kernel).
+int qmm_gemv_max_m();
 // The library's split-K workspace for operator-level calls (grown on demand,
 // zeroed when grown): kind 0 for the mma.sync kernels (which keep it zero),
 // kind 1 for the tensor-core kernel (which keeps only its counters zero).

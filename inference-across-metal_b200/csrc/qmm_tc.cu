@@ -80,19 +80,17 @@ __device__ __forceinline__ void dequant_group(const uint4& c0, const uint4& c1, 
     for (int s = 0; s < 4; ++s) r[4 * j + s] = dequant2(w[j] >> (4 * s), s2, b2);
 }
 
-// The same for a tile whose scales were stored times 2^130: the code moved to
-// bits 3-6 of each half is the bf16 subnormal q * 2^-130, and one packed FMA
-// gives bf16(q * scale + bias) with the product exact and one rounding.
+// The same for a tile whose scales were stored times 2^129 (qmm.cuh).
 __device__ __forceinline__ void dequant_group_fast(const uint4& c0, const uint4& c1, uint32_t sb, uint32_t (&r)[32]) {
   const uint32_t s2 = prmt(sb, sb, 0x1010u), b2 = prmt(sb, sb, 0x3232u);
   const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
+  for (int j = 0; j < 8; ++j) {
+    uint32_t v[4];
+    qp_codes_hi(w[j], v);
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const uint32_t v = s == 0 ? (w[j] << 3) : (w[j] >> (4 * s - 3));
-      r[4 * j + s] = fma_bf2(v & 0x00780078u, s2, b2);
-    }
+    for (int s = 0; s < 4; ++s) r[4 * j + s] = fma_bf2(v[s], s2, b2);
+  }
 }
 
 __device__ __forceinline__ float4 ld_cg_f4(const float* p) {
@@ -350,7 +348,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
       uint4 c[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        c[j] = *reinterpret_cast<const uint4*>(blk + row * 128 + (((4 * gp + j) ^ (row & 7)) << 4));
+        c[j] = *reinterpret_cast<const uint4*>(blk + row * 128 + (((4 * gp + j) ^ qp_swz(row)) << 4));
       const uint2 sb = *reinterpret_cast<const uint2*>(blk + kQpCodeBytes + row * 16 + gp * 8);
       __syncwarp();
       if (lane == 0) mbar_arrive(wempty(s));
@@ -521,14 +519,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------- packing
-// Clears the flag of every tile holding a scale that is not below 0.25 in
-// magnitude (bf16 exponent field >= 125, non-finite values included).
+// Clears the flag of every tile holding a scale that is not below 0.5 in
+// magnitude (bf16 exponent field >= 126, non-finite values included).
 __global__ void qmm_pack_scan_kernel(const uint16_t* __restrict__ s, int rows, int G, unsigned char* __restrict__ flags,
                                      int per_tile) {
   const long long total = static_cast<long long>(rows) * G;
   for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    if (((s[idx] >> 7) & 0xFF) >= 125) flags[(idx / G) / per_tile] = 0;
+    if (((s[idx] >> 7) & 0xFF) >= 126) flags[(idx / G) / per_tile] = 0;
   }
 }
 
@@ -557,7 +555,7 @@ __global__ void qmm_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* 
         }
         o[j] = p;
       }
-      *reinterpret_cast<uint4*>(blk + tr * 128 + ((c ^ (tr & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(blk + tr * 128 + ((c ^ qp_swz(tr)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
     const bool fast = flags[t] != 0;
     uint32_t sbv[4];
@@ -567,8 +565,8 @@ __global__ void qmm_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* 
       if (gg < G) {
         sc = s[static_cast<size_t>(r) * G + gg];
         bi = b[static_cast<size_t>(r) * G + gg];
-        // exact: |scale| < 0.25, so scale * 2^130 is a finite bf16 with the same digits
-        if (fast) sc = f2bf(ldexpf(bf2f(static_cast<uint16_t>(sc)), 130));
+        // exact: |scale| < 0.5, so scale * 2^129 is a finite bf16 with the same digits
+        if (fast) sc = f2bf(ldexpf(bf2f(static_cast<uint16_t>(sc)), 129));
       }
       sbv[g] = sc | (bi << 16);
     }

@@ -1,6 +1,9 @@
-"""Tensor-core W4A16 matmul (tcgen05, weights dequantized into tensor memory)
-through the C ABI: the packed weight layout byte for byte against a numpy
-restatement, and the matmul against the oracle restatement of MLX's qmm.
+"""The W4A16 matmul on packed weights through the C ABI: the packed weight
+layout byte for byte against a numpy restatement, and the matmul against the
+oracle restatement of MLX's qmm -- on the register-dequant GEMV kernel
+(mma.sync, passes of up to 16 tokens) and on the tensor-core kernel (tcgen05,
+weights dequantized into tensor memory; wider passes, or every pass with
+IAM_QMM_GEMV_MAX_M=0).
 
 Tolerance as for iam_qmm_affine4: both sides multiply x with the bf16 weights
 bf16(q * scale + bias); only the fp32 accumulation order differs, so relative
@@ -24,13 +27,18 @@ u = O.to_u16
 ROWS, BLOCK_K, CODE_BYTES, BLOCK_BYTES = 128, 256, 16384, 18432
 
 
+def swz(r):
+    """The chunk swizzle of qmm.cuh (qp_swz): a bijection of r % 8."""
+    return ((r & 3) << 1) | ((r >> 2) & 1)
+
+
 def pack_ref(w, s, b):
     """numpy restatement of the packed layout (qmm.cuh): tiles of 128 rows x
-    256 k, codes row-major with 16-byte chunks swizzled by (chunk ^ row % 8),
+    256 k, codes row-major with 16-byte chunks swizzled by (chunk ^ swz(row)),
     nibble s of a word = k 2s, nibble s+4 = k 2s+1; (scale | bias << 16) words
     after the codes; then one flag byte a tile (padded to 256 bytes): 1 when
-    every scale of the tile is below 0.25 in magnitude, and then the tile's
-    scales are stored times 2^130."""
+    every scale of the tile is below 0.5 in magnitude, and then the tile's
+    scales are stored times 2^129."""
     N, KW = w.shape
     K = KW * 8
     KB = -(-K // BLOCK_K)
@@ -44,10 +52,11 @@ def pack_ref(w, s, b):
     s16 = s.view(np.uint16)
     flags = np.ones(T, np.uint8)
     for t in range(T):
-        if np.any(((s16[t * ROWS:(t + 1) * ROWS] >> 7) & 0xFF) >= 125):
+        if np.any(((s16[t * ROWS:(t + 1) * ROWS] >> 7) & 0xFF) >= 126):
             flags[t] = 0
-    # 2^130 overflows float32 on its own; the products (|s| < 0.25) do not
-    s_big = (s.astype(np.float64) * 2.0 ** 130).astype(np.float32).astype(synth.BF16).view(np.uint16)
+    # the products (|s| < 0.5) stay below the float32 and bf16 maxima
+    with np.errstate(over="ignore"):
+        s_big = (s.astype(np.float64) * 2.0 ** 129).astype(np.float32).astype(synth.BF16).view(np.uint16)
     s_st = np.where(np.repeat(flags, ROWS)[:N, None] == 1, s_big, s16)
     sb = np.zeros((N, KB * 4), np.uint32)
     sb[:, :G] = s_st.astype(np.uint32) | (b.view(np.uint16).astype(np.uint32) << 16)
@@ -57,7 +66,7 @@ def pack_ref(w, s, b):
             blk = out[t, kb]
             chunks = words[r, kb * 32:(kb + 1) * 32].reshape(8, 4)
             for c in range(8):
-                o = tr * 128 + ((c ^ (tr & 7)) << 4)
+                o = tr * 128 + ((c ^ swz(tr)) << 4)
                 blk[o:o + 16] = chunks[c].view(np.uint8)
             blk[CODE_BYTES + tr * 16:CODE_BYTES + tr * 16 + 16] = sb[r, kb * 4:kb * 4 + 4].view(np.uint8)
     tail = np.zeros(-(-T // 256) * 256, np.uint8)
@@ -76,10 +85,10 @@ def pack_dev(w, s, b, N, K):
 
 
 def big_scales(s, rows):
-    """Scales of `rows` raised to 0.3 in one group each: those tiles take the
-    general conversion (no 2^130 pre-scaling)."""
+    """Scales of `rows` raised to 0.6 in one group each: those tiles take the
+    general conversion (no 2^129 pre-scaling)."""
     s = s.copy()
-    s[rows, 1] = synth.BF16(0.3)
+    s[rows, 1] = synth.BF16(0.6)
     return s
 
 
@@ -97,10 +106,19 @@ def test_pack_layout_matches_restatement():
     assert np.array_equal(got, ref)
 
 
-@pytest.mark.parametrize("M", [1, 32, 64])
-def test_qmm_packed_mixed_tiles(M):
-    """Tiles with a scale >= 0.25 use the general conversion, the others the
-    2^130 pre-scaled one; both must match the oracle."""
+@pytest.fixture(params=["default", "tensor_core"])
+def kernel(request, monkeypatch):
+    """The library's kernel choice (GEMV up to 16 tokens), or the tensor-core
+    kernel at every width."""
+    if request.param == "tensor_core":
+        monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "0")
+    return request.param
+
+
+@pytest.mark.parametrize("M", [1, 8, 16, 32, 64])
+def test_qmm_packed_mixed_tiles(M, kernel):
+    """Tiles with a scale >= 0.5 use the general conversion, the others the
+    2^129 pre-scaled one; both must match the oracle."""
     N, K = 512, 1024
     w, s, b = synth.gen_qweight(61, "t.tc.mixed", N, K)
     s = big_scales(s, [5, 300])  # tiles 0 and 2
@@ -131,29 +149,32 @@ def _case(N, K, M, indep_bias=False, seed=31):
 
 
 @pytest.mark.parametrize("N,K", [(10240, 5120), (6144, 5120), (48, 5120), (5120, 6144), (1024, 5120)])
-@pytest.mark.parametrize("M", [1, 3, 8, 16, 17, 32, 40, 64, 100])
-def test_qmm_packed_matches_oracle(N, K, M):
+@pytest.mark.parametrize("M", [1, 2, 3, 8, 9, 16, 17, 32, 40, 64, 100])
+def test_qmm_packed_matches_oracle(N, K, M, kernel):
     got, ref = _case(N, K, M)
     assert_close_bf16(got, ref)
 
 
-@pytest.mark.parametrize("N,K,M", [(5120, 17408, 4), (5120, 17408, 32), (264, 704, 5), (128, 256, 1)])
-def test_qmm_packed_odd_shapes(N, K, M):
+@pytest.mark.parametrize("N,K,M", [(5120, 17408, 4), (5120, 17408, 16), (5120, 17408, 32), (264, 704, 5),
+                                   (128, 256, 1), (136, 448, 12)])
+def test_qmm_packed_odd_shapes(N, K, M, kernel):
     got, ref = _case(N, K, M, indep_bias=True, seed=41)
     assert_close_bf16(got, ref)
 
 
-def test_qmm_packed_repeat_is_deterministic():
-    """Split-K partials meet in a workspace the last CTA re-zeroes: a second
-    call must give the same bits."""
+@pytest.mark.parametrize("M", [4, 32])
+def test_qmm_packed_repeat_is_deterministic(M):
+    """Split-K partials meet in a workspace whose counters the last CTA
+    re-zeroes, summed in split order: a second call must give the same bits
+    (GEMV kernel at 4 tokens, tensor-core kernel at 32)."""
     w, s, b = synth.gen_qweight(51, "t.tc.rep", 1024, 6144)
-    x = synth.gen_normal_bf16(52, "t.tc.rep.x", 32 * 6144, 1.0).reshape(32, 6144)
+    x = synth.gen_normal_bf16(52, f"t.tc.rep.x{M}", M * 6144, 1.0).reshape(M, 6144)
     packed = pack_dev(w, s, b, 1024, 6144)
     dx = dev(x.view(np.uint16), torch)
     ys = []
     for _ in range(2):
-        y = empty_u16(torch, 32, 1024)
-        I.qmm_affine4_packed(ptr(packed), ptr(dx), ptr(y), 32, 1024, 6144)
+        y = empty_u16(torch, M, 1024)
+        I.qmm_affine4_packed(ptr(packed), ptr(dx), ptr(y), M, 1024, 6144)
         torch.cuda.synchronize()
         ys.append(host_u16(y))
     assert np.array_equal(ys[0], ys[1])

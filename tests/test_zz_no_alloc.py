@@ -41,17 +41,16 @@ def test_noalloc_matches_qmm_affine4_twice(N, K, M):
         assert_close_bf16(got, oracle)
 
 
-def test_noalloc_rejects_shapes_beyond_its_scratch():
+def test_noalloc_rejects_shapes_beyond_its_scratch(monkeypatch):
     """A plan whose split-K scratch exceeds the fixed array is an IAM_EINVAL,
-    reported before anything is launched (the pointers are never read)."""
-    big = None
-    for N, K, M in ((4096, 65536, 32), (8192, 131072, 32), (16384, 131072, 32)):
-        ks, nf, nc = I.qmm_affine4_plan(M, N, K)
-        if nf > 1 << 20 or nc > 16384:
-            big = (N, K, M)
-            break
-    assert big is not None, "no candidate shape exceeds the fixed scratch"
-    N, K, M = big
+    reported before anything is launched (the pointers are never read).  The
+    library's own planner splits K only for matrices too narrow to fill the
+    GPU, whose scratch fits; a plan forced to split K four ways over 65536
+    rows of 32 tokens (IAM_QMM_CFG, the planner override) needs 2 Mi floats."""
+    monkeypatch.setenv("IAM_QMM_CFG", "8,4")
+    N, K, M = 65536, 5120, 32
+    ks, nf, nc = I.qmm_affine4_plan(M, N, K)
+    assert ks == 4 and nf > 1 << 20, (ks, nf, nc)
     with pytest.raises(I.IamError) as err:
         I.qmm_affine4_noalloc(16, 16, 16, 16, 16, M, N, K)
     assert err.value.status == I.IAM_EINVAL
