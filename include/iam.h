@@ -101,6 +101,18 @@ int iam_qmm_pack_affine4(const uint32_t* w, const uint16_t* s, const uint16_t* b
 int iam_qmm_affine4_packed(const void* packed, const uint16_t* x, uint16_t* y, int M, int N, int K,
                            void* stream);
 
+/* iam_qmm_affine4_packed run synchronously with its device-side waits
+ * checked: every wait inside the kernel that may give up polls at most
+ * `wait_limit` times (0: the library default, about a second), and a wait
+ * that gave up makes the call return IAM_ETIMEOUT after the kernel has
+ * drained its copies and exited (the context stays usable; y is then not
+ * written).  `starve` != 0 is fault injection for tests: the kernel issues
+ * none of its copies, so its first wait is on a phase that nothing completes.
+ * No counterpart in the reference, whose only check is the command-buffer
+ * status after waitUntilCompleted (full_forward.swift:1242-1245). */
+int iam_qmm_affine4_packed_checked(const void* packed, const uint16_t* x, uint16_t* y, int M, int N, int K,
+                                   int wait_limit, int starve, void* stream);
+
 /* rms_norm_bf16 (full_forward.swift:59-86), applied to each of `rows` rows. */
 int iam_rms_norm_bf16(const uint16_t* x, const uint16_t* weight, uint16_t* out, int rows, int dim,
                       float eps, void* stream);
@@ -220,6 +232,9 @@ typedef struct iam_dims {
   int max_ctx;           /* KV-cache capacity in tokens */
   int max_rows;          /* largest verify width (tokens per step, all sequences) */
   int max_seqs;          /* sequence slots for iam_verify_batch (1: one sequence) */
+  int comm_timeout_ms;   /* world > 1: bound on the communicator set-up and on each synchronous
+                            step's wait for its collectives (0: 120000); past it the communicator
+                            is aborted and the call returns IAM_ETIMEOUT */
 } iam_dims;
 
 /* Qwen3.5-27B defaults (full_forward.swift:18-49). */
@@ -355,6 +370,17 @@ int iam_verify_batch_device(iam_engine* e, const int32_t* d_tokens, int n_seq, i
 /* Device-resident variant for benchmarking: tokens/outputs stay on the GPU
  * (d_tokens int32 [K], d_argmax int32 [K]) and nothing is synchronised. */
 int iam_verify_device(iam_engine* e, const int32_t* d_tokens, int K, int pos, int32_t* d_argmax, void* stream);
+
+/* The device-side status of the engine's steps so far, for the variants that
+ * do not synchronise: waits for `stream` (NULL: the engine's) and the engine
+ * stream, then returns IAM_OK, IAM_ETIMEOUT (a bounded wait inside a kernel
+ * gave up), IAM_EINVAL (a token id out of range reached the embedding) or,
+ * across GPUs, the communicator's failure (IAM_ENCCL / IAM_ETIMEOUT past
+ * comm_timeout_ms, with the communicator aborted).  The word is cleared.
+ * iam_verify and iam_verify_batch return the same statuses by themselves.
+ * No counterpart in the reference (full_forward.swift:1242-1245 checks the
+ * command-buffer status only). */
+int iam_engine_status(iam_engine* e, void* stream);
 
 /* Read back device copies of internal tensors for tests (host buffers).
  * State tensors ("state.S.<layer>", "state.conv.<layer>",

@@ -16,11 +16,13 @@
 // an argmax epilogue and the accept-length finalisation.
 #include <dlfcn.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <map>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "kernels.cuh"
@@ -168,6 +170,7 @@ struct EngineImpl {
   int* d_err = nullptr;
   StepIn* h_in = nullptr;
   int32_t* h_out = nullptr;
+  int* h_err = nullptr;  // pinned mirror of d_err, read with every synchronous step
 
   // multi-sequence steps: positions [max_seqs] then tokens [max_rows] (d_bin,
   // pinned mirror h_bin); accept lengths [max_seqs] then argmax [max_rows]
@@ -474,6 +477,8 @@ int alloc_all(EngineImpl& e) {
   E_CUDA(cudaMemset(e.d_err, 0, sizeof(int)));
   E_CUDA(cudaMallocHost(&e.h_in, sizeof(int32_t) * (1 + R)));
   E_CUDA(cudaMallocHost(&e.h_out, sizeof(int32_t) * (1 + R)));
+  E_CUDA(cudaMallocHost(&e.h_err, sizeof(int)));
+  *e.h_err = 0;
   E_CUDA(cudaMalloc(&e.d_bin, sizeof(int32_t) * (slots + R)));
   E_CUDA(cudaMemset(e.d_bin, 0, sizeof(int32_t) * (slots + R)));
   E_CUDA(cudaMalloc(&e.d_bout, sizeof(int32_t) * (slots + R)));
@@ -562,6 +567,7 @@ int run_qmm(EngineImpl& e, QmmArgs& a, const char* kind, double bytes) {
   Recorder rec(e, kind, bytes);
   a.ws = e.qws;
   a.counters = e.qctr;
+  a.err = e.d_err;
   return qmm_run(a, e.stream, e.pdl, e.qws_floats, e.qctr_n);
 }
 
@@ -1057,6 +1063,8 @@ extern "C" int iam_tp_shard_of(const iam_dims* dims, int rank, int world, iam_tp
 
 extern "C" int iam_nccl_unique_id(void* id128) { return iam::nccl_unique_id(id128); }
 
+static int comm_timeout_ms(const iam::EngineImpl& e) { return e.d.comm_timeout_ms > 0 ? e.d.comm_timeout_ms : 120000; }
+
 extern "C" int iam_create(const iam_dims* dims, int device, int rank, int world, const void* nccl_id,
                           iam_engine** out) {
   using namespace iam;
@@ -1084,7 +1092,7 @@ extern "C" int iam_create(const iam_dims* dims, int device, int rank, int world,
   if (r == IAM_OK) r = gdn_init_attrs();  // kernel attributes before any graph capture
   if (r == IAM_OK) r = attn_init_attrs();
   if (r == IAM_OK) r = alloc_all(e);
-  if (r == IAM_OK && world > 1) r = nccl_init(&e.comm, nccl_id, rank, world);
+  if (r == IAM_OK && world > 1) r = nccl_init(&e.comm, nccl_id, rank, world, comm_timeout_ms(e));
   if (r != IAM_OK) {
     iam_destroy(eng);
     return r;
@@ -1109,7 +1117,7 @@ extern "C" void iam_destroy(iam_engine* eng) {
   for (void* p : bufs)
     if (p) cudaFree(p);
   for (void* p : {static_cast<void*>(e.h_in), static_cast<void*>(e.h_out), static_cast<void*>(e.h_bin),
-                  static_cast<void*>(e.h_bout)})
+                  static_cast<void*>(e.h_bout), static_cast<void*>(e.h_err)})
     if (p) cudaFreeHost(p);
   if (e.stream) cudaStreamDestroy(e.stream);
   delete eng;
@@ -1609,12 +1617,58 @@ extern "C" int iam_state_init(iam_engine* eng, uint64_t seed, int ctx) {
   return IAM_OK;
 }
 
+// After a synchronous step: the device error word (a bounded wait that gave
+// up, a token id out of range) becomes the call's status; the word is
+// cleared for the next step.  h_err was filled by a copy enqueued after the
+// step and before the synchronisation.
+static int device_status(iam::EngineImpl& e, const char* what) {
+  using namespace iam;
+  const int st = *e.h_err;
+  if (st == IAM_OK) return IAM_OK;
+  *e.h_err = 0;
+  E_CUDA(cudaMemsetAsync(e.d_err, 0, sizeof(int), e.stream));
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  return e.setf(st, std::string(what) + ": device-side error " + iam_status_string(st) +
+                        (st == IAM_ETIMEOUT ? " (a bounded wait inside a kernel gave up)" : ""));
+}
+
+// Waits for the engine stream.  With one GPU a plain synchronisation; across
+// GPUs the host polls the stream, the communicator's asynchronous error and a
+// deadline (comm_timeout_ms): a peer that failed or left makes the call end
+// in IAM_ENCCL / IAM_ETIMEOUT, with the communicator aborted (its kernels in
+// flight return) instead of a hang.  After that the engine refuses steps.
+static int sync_step(iam::EngineImpl& e, const char* what) {
+  using namespace iam;
+  if (e.world == 1 || !e.comm) {
+    E_CUDA(cudaStreamSynchronize(e.stream));
+    return IAM_OK;
+  }
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(comm_timeout_ms(e));
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(e.stream);
+    if (q == cudaSuccess) return IAM_OK;
+    if (q != cudaErrorNotReady) E_CUDA(q);
+    int st = nccl_async_status(e.comm);
+    if (st == IAM_OK && std::chrono::steady_clock::now() > deadline) st = IAM_ETIMEOUT;
+    if (st != IAM_OK) {
+      nccl_abort(e.comm);
+      e.comm = nullptr;
+      cudaStreamSynchronize(e.stream);  // the aborted collectives return
+      return e.setf(st, std::string(what) + (st == IAM_ETIMEOUT ? ": the step's collectives did not finish within "
+                                                                  "comm_timeout_ms; communicator aborted"
+                                                                : ": communicator failed and was aborted"));
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
 static int verify_common(iam_engine* eng, int K, int pos) {
   using namespace iam;
   IAM_CHECK(eng, "iam_verify: null engine");
   EngineImpl& e = eng->impl;
   IAM_CHECK(K >= 1 && K <= e.d.max_rows && K <= kMaxRowsFinalize, "iam_verify: K out of range (1..max_rows, <= 256)");
   IAM_CHECK(pos >= 0 && pos + K <= e.d.max_ctx, "iam_verify: pos + K exceeds max_ctx");
+  if (e.world > 1 && !e.comm) return e.setf(IAM_ESTATE, "iam_verify: the communicator was aborted");
   E_CUDA(cudaSetDevice(e.device));
   E_RUN(ensure_packed(e));
   return IAM_OK;
@@ -1639,7 +1693,9 @@ extern "C" int iam_verify(iam_engine* eng, const int32_t* tokens, int K, int pos
   E_CUDA(cudaGraphLaunch(g, e.stream));
   e.last_K = K;
   E_CUDA(cudaMemcpyAsync(e.h_out, e.d_out, sizeof(int32_t) * (1 + K), cudaMemcpyDeviceToHost, e.stream));
-  E_CUDA(cudaStreamSynchronize(e.stream));
+  E_CUDA(cudaMemcpyAsync(e.h_err, e.d_err, sizeof(int), cudaMemcpyDeviceToHost, e.stream));
+  E_RUN(sync_step(e, "iam_verify"));
+  E_RUN(device_status(e, "iam_verify"));
   std::memcpy(argmax_out, e.h_out + 1, sizeof(int32_t) * K);
   if (accept_len) *accept_len = e.h_out[0];
   return IAM_OK;
@@ -1692,6 +1748,7 @@ extern "C" int iam_verify_device(iam_engine* eng, const int32_t* d_tokens, int K
   EngineImpl& e = eng->impl;
   if (K < 1 || K > e.d.max_rows || K > kMaxRowsFinalize)
     return e.setf(IAM_EINVAL, "iam_verify_device: K out of range (1..max_rows, <= 256)");
+  if (e.world > 1 && !e.comm) return e.setf(IAM_ESTATE, "iam_verify_device: the communicator was aborted");
   cudaStream_t st = stream ? as_stream(stream) : e.stream;
   cudaGraphExec_t g = nullptr;
   E_RUN(get_graph(e, K, &g));
@@ -1734,6 +1791,7 @@ static int batch_common(iam_engine* eng, int n_seq, int K) {
   if (n_seq < 1 || n_seq > e.max_seqs) return e.setf(IAM_EINVAL, "iam_verify_batch: n_seq out of range (1..max_seqs)");
   if (K < 1 || static_cast<long long>(n_seq) * K > e.d.max_rows)
     return e.setf(IAM_EINVAL, "iam_verify_batch: n_seq * K exceeds max_rows");
+  if (e.world > 1 && !e.comm) return e.setf(IAM_ESTATE, "iam_verify_batch: the communicator was aborted");
   E_CUDA(cudaSetDevice(e.device));
   E_RUN(ensure_packed(e));
   return IAM_OK;
@@ -1764,7 +1822,9 @@ extern "C" int iam_verify_batch(iam_engine* eng, const int32_t* tokens, int n_se
   E_CUDA(cudaMemcpyAsync(e.h_bout, e.d_bout, sizeof(int32_t) * n_seq, cudaMemcpyDeviceToHost, e.stream));
   E_CUDA(cudaMemcpyAsync(e.h_bout + e.max_seqs, e.d_bout + e.max_seqs, sizeof(int32_t) * rows,
                          cudaMemcpyDeviceToHost, e.stream));
-  E_CUDA(cudaStreamSynchronize(e.stream));
+  E_CUDA(cudaMemcpyAsync(e.h_err, e.d_err, sizeof(int), cudaMemcpyDeviceToHost, e.stream));
+  E_RUN(sync_step(e, "iam_verify_batch"));
+  E_RUN(device_status(e, "iam_verify_batch"));
   std::memcpy(argmax_out, e.h_bout + e.max_seqs, sizeof(int32_t) * rows);
   if (accept_len) std::memcpy(accept_len, e.h_bout, sizeof(int32_t) * n_seq);
   return IAM_OK;
@@ -1789,6 +1849,25 @@ extern "C" int iam_verify_batch_device(iam_engine* eng, const int32_t* d_tokens,
     E_CUDA(cudaMemcpyAsync(d_argmax, e.d_bout + e.max_seqs, sizeof(int32_t) * rows, cudaMemcpyDeviceToDevice, st));
   if (d_accept) E_CUDA(cudaMemcpyAsync(d_accept, e.d_bout, sizeof(int32_t) * n_seq, cudaMemcpyDeviceToDevice, st));
   return IAM_OK;
+}
+
+extern "C" int iam_engine_status(iam_engine* eng, void* stream) {
+  using namespace iam;
+  IAM_CHECK(eng, "iam_engine_status: null engine");
+  EngineImpl& e = eng->impl;
+  E_CUDA(cudaSetDevice(e.device));
+  const cudaStream_t st = stream ? as_stream(stream) : e.stream;
+  if (st != e.stream) {  // order the engine stream after the caller's
+    cudaEvent_t ev = nullptr;
+    E_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    const cudaError_t a = cudaEventRecord(ev, st);
+    const cudaError_t b = a == cudaSuccess ? cudaStreamWaitEvent(e.stream, ev, 0) : a;
+    cudaEventDestroy(ev);
+    E_CUDA(b);
+  }
+  E_CUDA(cudaMemcpyAsync(e.h_err, e.d_err, sizeof(int), cudaMemcpyDeviceToHost, e.stream));
+  E_RUN(sync_step(e, "iam_engine_status"));
+  return device_status(e, "iam_engine_status");
 }
 
 extern "C" int iam_read_hidden(iam_engine* eng, uint16_t* host_ptr, int K) {

@@ -49,6 +49,13 @@ struct QmmArgs {
   float* ws;      // split-K partial sums (zero between launches)
   int* counters;  // split-K arrival counters (zero between launches)
   int* err;       // device error word (a bounded wait that gave up writes IAM_ETIMEOUT)
+  // Poll budget of every wait that may give up (0: the library default).
+  // Waits for copies or MMAs already in flight always get the full budget.
+  int wait_limit;
+  // Fault injection for tests: the producer issues no copies at all, so the
+  // consumers' first wait is on a phase that nothing completes and must run
+  // out (nothing is in flight when the CTA exits).
+  int starve;
   QmmSeg seg[kQmmMaxSeg];
 };
 

@@ -158,6 +158,8 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
     *abort_flag = 1;
     if (A.err) atomicExch(A.err, IAM_ETIMEOUT);
   };
+  // budget of the waits that may give up; waits for copies in flight get the full one
+  const uint32_t lim = wait_limit(A.wait_limit);
 
   if (warp == kGvWarps) {
     // ------------------------------------------------------------ producer
@@ -175,14 +177,16 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
         for (int b = 0; b < 4; ++b)
           tma_load_2d(sbase + s * L::kStage + b * L::kXBox, &T.xmap, (kb0 + i) * kQpBlockK + 64 * b, 0, full(s));
       };
-      const int first = min(nkb, S);
+      // (a starved launch, a test's fault injection, issues nothing: the
+      // consumers' first wait can only run out)
+      const int first = A.starve ? 0 : min(nkb, S);
       for (int i = 0; i < first; ++i) load_w(i);  // weights do not depend on the preceding kernel
       pdl_wait();
       for (int i = 0; i < first; ++i) load_x(i);
       int issued = first;
-      for (; issued < nkb; ++issued) {
+      for (; !A.starve && issued < nkb; ++issued) {
         const int s = issued % S;
-        if (!mbar_wait(empty(s), ((issued / S) - 1) & 1, abort_flag)) {
+        if (!mbar_wait(empty(s), ((issued / S) - 1) & 1, abort_flag, lim)) {
           give_up();
           break;
         }
@@ -246,7 +250,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
     uint32_t phase = 0;
     int s = 0;
     for (int i = 0; i < nkb; ++i) {
-      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(full(s), phase, abort_flag))) return false;
+      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(full(s), phase, abort_flag, lim))) return false;
       const unsigned char* stg = smem + s * L::kStage;
       uint4 xr[2][2][NT];
 #pragma unroll

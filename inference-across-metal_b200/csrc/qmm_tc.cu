@@ -230,6 +230,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     *abort_flag = 1;
     if (A.err) atomicExch(A.err, IAM_ETIMEOUT);
   };
+  // budget of the waits that may give up; waits for work in flight get the full one
+  const uint32_t lim = wait_limit(A.wait_limit);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -250,13 +252,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         for (int b = 0; b < 4; ++b)
           tma_load_2d(xs + b * L::kXBox, &T.xmap, (kb0 + i) * kQpBlockK + 64 * b, 0, xfull(s));
       };
-      int iw = min(nkb, WS), ix = min(nkb, XS);
+      // (a starved launch, a test's fault injection, issues nothing: the
+      // consumers' first waits can only run out)
+      int iw = A.starve ? 0 : min(nkb, WS), ix = A.starve ? 0 : min(nkb, XS);
       // weights do not depend on the preceding kernel: start them first
       for (int i = 0; i < iw; ++i) load_w(i);
       pdl_wait();
       for (int i = 0; i < ix; ++i) load_x(i);
       uint32_t idle = 0;
-      while (iw < nkb || ix < nkb) {
+      while (!A.starve && (iw < nkb || ix < nkb)) {
         bool progress = false;
         if (iw < nkb && mbar_test(wempty(iw % WS), ((iw / WS) - 1) & 1)) {
           load_w(iw++);
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
         if (progress) {
           idle = 0;
         } else {
-          if (++idle > kMbarSpinLimit || *abort_flag) {
+          if (++idle > lim || *abort_flag) {
             give_up();
             break;
           }
@@ -295,8 +299,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     Ring<XS> xr;
     for (int i = 0; i < nkb; ++i, ar.next(), xr.next()) {
       const int slot = ar.idx, xsl = xr.idx;
-      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(xfull(xsl), xr.phase, abort_flag) &&
-                                       mbar_wait_light(afull(slot), ar.phase, abort_flag))) {
+      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(xfull(xsl), xr.phase, abort_flag, lim) &&
+                                       mbar_wait_light(afull(slot), ar.phase, abort_flag, lim))) {
         ok = false;
         break;
       }
@@ -340,7 +344,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     for (int i = team; i < nkb; i += 2, wr.next2(), ar.next2()) {
       const int s = wr.idx;
       // every branch below is warp-uniform: tcgen05.st/ld need the whole warp
-      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(wfull(s), wr.phase, abort_flag))) {
+      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(wfull(s), wr.phase, abort_flag, lim))) {
         give_up();
         break;
       }
@@ -353,7 +357,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive(wempty(s));
       const int slot = ar.idx;
-      if (!__all_sync(0xffffffffu, ar.first_lap || mbar_wait_light(aempty(slot), ar.phase ^ 1u, abort_flag))) {
+      if (!__all_sync(0xffffffffu, ar.first_lap || mbar_wait_light(aempty(slot), ar.phase ^ 1u, abort_flag, lim))) {
         give_up();
         break;
       }
@@ -765,4 +769,45 @@ extern "C" int iam_qmm_affine4_packed(const void* packed, const uint16_t* x, uin
   a.seg[0].rows = N;
   a.seg[0].mode = EPI_STORE;
   return qmm_run(a, as_stream(stream), false);
+}
+
+extern "C" int iam_qmm_affine4_packed_checked(const void* packed, const uint16_t* x, uint16_t* y, int M, int N,
+                                              int K, int wait_limit, int starve, void* stream) {
+  using namespace iam;
+  IAM_CHECK(N > 0 && N % 8 == 0, "iam_qmm_affine4_packed_checked: N must be a positive multiple of 8");
+  IAM_CHECK(packed && x && y, "iam_qmm_affine4_packed_checked: null pointer");
+  IAM_CHECK(wait_limit >= 0, "iam_qmm_affine4_packed_checked: wait_limit must be >= 0");
+  const cudaStream_t st = as_stream(stream);
+  int* d_status = nullptr;
+  IAM_CUDA(cudaMalloc(&d_status, sizeof(int)));
+  int h_status = 0;
+  int r = IAM_OK;
+  cudaError_t ce = cudaMemsetAsync(d_status, 0, sizeof(int), st);
+  if (ce == cudaSuccess) {
+    QmmArgs a = {};
+    a.x = x;
+    a.ldx = K;
+    a.M = M;
+    a.K = K;
+    a.nseg = 1;
+    a.err = d_status;
+    a.wait_limit = wait_limit;
+    a.starve = starve ? 1 : 0;
+    a.seg[0].packed = static_cast<const unsigned char*>(packed);
+    a.seg[0].out = y;
+    a.seg[0].ldo = N;
+    a.seg[0].rows = N;
+    a.seg[0].mode = EPI_STORE;
+    r = qmm_run(a, st, false);
+    if (r == IAM_OK) {
+      ce = cudaMemcpyAsync(&h_status, d_status, sizeof(int), cudaMemcpyDeviceToHost, st);
+      if (ce == cudaSuccess) ce = cudaStreamSynchronize(st);
+    }
+  }
+  cudaFree(d_status);
+  if (r != IAM_OK) return r;
+  IAM_CUDA(ce);
+  if (h_status != IAM_OK)
+    return fail(h_status, "iam_qmm_affine4_packed_checked: a bounded wait inside the matmul gave up");
+  return IAM_OK;
 }

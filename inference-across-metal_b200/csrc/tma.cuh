@@ -12,6 +12,12 @@ namespace iam {
 
 constexpr uint32_t kMbarSpinLimit = 1u << 22;
 
+// The poll budget of a wait that may give up: a kernel argument of 0 means
+// the library default.
+__device__ __forceinline__ uint32_t wait_limit(int arg) {
+  return arg > 0 ? static_cast<uint32_t>(arg) : kMbarSpinLimit;
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -33,8 +39,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 // after one wait gave up, the others end promptly instead of each spending
 // its own budget.  Waits for copies or MMAs already in flight pass no abort
 // flag -- those complete by themselves and must before the CTA exits.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase, const volatile int* abort = nullptr) {
-  for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase, const volatile int* abort = nullptr,
+                                          uint32_t limit = kMbarSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -63,8 +70,9 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 // accesses after the barrier with a lightweight acquire fence.  Cheaper per
 // poll (about 100 cycles instead of about 400), for threads whose issue rate
 // matters (a tensor-core issuer).
-__device__ __forceinline__ bool mbar_wait_light(uint32_t bar, uint32_t phase, const volatile int* abort = nullptr) {
-  for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+__device__ __forceinline__ bool mbar_wait_light(uint32_t bar, uint32_t phase, const volatile int* abort = nullptr,
+                                                uint32_t limit = kMbarSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.relaxed.cta.shared::cta.b64 p, [%1], %2;\n"

@@ -28,6 +28,8 @@ _SIGS = {
     "iam_version": (_i, []),
     "iam_qmm_affine4": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "iam_qmm_affine4_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "iam_qmm_affine4_packed_checked": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
+    "iam_engine_status": (_i, [_vp, _vp]),
     "iam_qmm_affine4_plan": (_i, [_i, _i, _i, C.POINTER(C.c_int), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "iam_qmm_packed_bytes": (_sz, [_i, _i]),
     "iam_qmm_pack_affine4": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
@@ -131,6 +133,10 @@ def qmm_affine4_plan(M, N, K):
     return ks.value, nf.value, nc.value
 
 
+def qmm_affine4_packed_checked(packed, x, y, M, N, K, wait_limit=0, starve=False, stream=None):
+    _check(lib().iam_qmm_affine4_packed_checked(packed, x, y, M, N, K, wait_limit, int(bool(starve)), _s(stream)))
+
+
 def qmm_packed_bytes(N, K) -> int:
     return int(lib().iam_qmm_packed_bytes(N, K))
 
@@ -212,7 +218,7 @@ class Dims(C.Structure):
     _fields_ = [(n, C.c_float if n in ("rope_theta", "eps") else C.c_int) for n in (
         "hidden", "intermediate", "vocab", "n_layers", "full_attn_interval", "n_heads", "n_kv_heads", "head_dim",
         "rotary_dim", "rope_theta", "gdn_k_heads", "gdn_v_heads", "gdn_dk", "gdn_dv", "conv_kernel", "group_size",
-        "eps", "max_ctx", "max_rows", "max_seqs")]
+        "eps", "max_ctx", "max_rows", "max_seqs", "comm_timeout_ms")]
 
     @classmethod
     def qwen35_27b(cls, **over):
@@ -352,6 +358,10 @@ class Engine:
         buf = np.empty(nbytes, np.uint8)
         self._c(lib().iam_read_tensor(self._h, name.encode(), buf.ctypes.data_as(C.c_void_p), nbytes))
         return buf
+
+    def status(self, stream=None):
+        """iam_engine_status: raises IamError for a device-side failure so far."""
+        self._c(lib().iam_engine_status(self._h, _s(stream)))
 
     def read_hidden(self, K: int):
         import numpy as np
