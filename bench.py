@@ -335,6 +335,30 @@ def profile_step(args):
     e.close()
 
 
+def profile_small(args):
+    """Two graph steps of a 4-layer full-width model (3 GDN + 1 attention
+    layer, vocab 32768, context 1024: about 2.5 GB on the device) at verify
+    width --k: the small case for per-kernel ncu captures of the GDN,
+    attention, RMSNorm and matmul kernels at the 27B layer sizes."""
+    import numpy as np
+    import torch
+    import iam_b200 as I
+    K = args.k
+    d = I.Dims.qwen35_27b(n_layers=4, vocab=32768, max_ctx=CTX + 4 * K + 64, max_rows=max(K, 32))
+    e = I.Engine(d)
+    e.init_synthetic(SEED)
+    e.state_init(SEED, CTX)
+    toks = torch.from_numpy(np.random.default_rng(0).integers(0, d.vocab, K).astype(np.int32)).cuda()
+    out = torch.zeros(K, dtype=torch.int32, device="cuda")
+    st = torch.cuda.Stream()
+    for _ in range(2):
+        e.verify_device(toks.data_ptr(), K, CTX, out.data_ptr(), st.cuda_stream)
+    torch.cuda.synchronize()
+    e.status()
+    print(json.dumps({"profile_small": K, "launches_per_step": e.step_launches(K)}))
+    e.close()
+
+
 def run_batch(args, rank, world, local_rank):
     """Multi-sequence verify: --batch sequences x --k draft tokens per step,
     each sequence in its own slot (seeded GDN state, conv window, --ctx prior
@@ -591,6 +615,8 @@ def main():
     ap.add_argument("--impl", default="iam")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--profile-step", action="store_true", help="two graph steps at --k, for ncu launch lists")
+    ap.add_argument("--profile-small", action="store_true",
+                    help="two graph steps of a 4-layer full-width model at --k, for per-kernel ncu captures")
     ap.add_argument("--profile-qmm", default=None,
                     help="N,K,M[,mlx];...: a few launches of each matmul (tensor-core, or mma.sync on the MLX layout), for ncu")
     ap.add_argument("--sweep", default=None, help="K1,K2,...: step time per verify width on one GPU")
@@ -605,6 +631,8 @@ def main():
         return qmm_sweep(args)
     if args.profile_step:
         return profile_step(args)
+    if args.profile_small:
+        return profile_small(args)
     if args.profile_qmm:
         return profile_qmm(args)
     args.warmup = max(args.warmup, 1)

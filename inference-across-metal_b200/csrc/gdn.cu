@@ -188,11 +188,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   const size_t hoff = static_cast<size_t>(h) * kHD * kHD;
   const int row0 = jr * R + warp * RPW;  // this warp's first state row
 
-  // The state does not depend on the preceding kernel: load it before waiting.
+  // The state, the conv window, the conv and norm weights do not depend on
+  // the preceding kernel (the window and state were written by the previous
+  // step): load them before waiting for it.
   float S[RPW][4];
   load_state<RPW>(S, S_rd + hoff, row0, lane);
-  pdl_wait();
-  pdl_trigger();
   const uint16_t* conv_in = (swap ? a.conv_out : a.conv_in) + coff;
   uint16_t* conv_out = (swap ? const_cast<uint16_t*>(a.conv_in) : a.conv_out) + coff;
 
@@ -223,6 +223,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
     w1 = conv_in[a.conv_dim + col];
     w2 = conv_in[2 * a.conv_dim + col];
   }
+  // this lane's four gated-norm weights (phase D: lanes < R / 4)
+  uint2 ww = make_uint2(0u, 0u);
+  if (lane < R / 4) ww = *reinterpret_cast<const uint2*>(a.norm_w + jr * R + 4 * lane);
+  pdl_wait();
+  pdl_trigger();
 
   int chunk = 0;
   for (int t0 = 0; t0 < a.rows; t0 += kChunk, ++chunk) {
@@ -306,7 +311,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
         const size_t row = static_cast<size_t>(t0 + t);
         const int d0 = jr * R + 4 * lane;
         const uint2 zz = *reinterpret_cast<const uint2*>(in + row * a.ld_in + a.z_col + h * kHD + d0);
-        const uint2 ww = *reinterpret_cast<const uint2*>(a.norm_w + d0);
         const float o0 = silu_f(lo_bf(zz.x)) * ((y.x / rms) * lo_bf(ww.x));
         const float o1 = silu_f(hi_bf(zz.x)) * ((y.y / rms) * hi_bf(ww.x));
         const float o2 = silu_f(lo_bf(zz.y)) * ((y.z / rms) * lo_bf(ww.y));

@@ -158,6 +158,7 @@ int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_
 // Register-dequant matmul over packed segments for narrow passes (M <= 16):
 // mma.sync on weights converted in registers, no tensor memory.
 constexpr int kGemvMaxM = 16;
+constexpr int kGemvDefaultMaxM = 8;
 int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap);
 // Widest pass that qmm_run sends to the GEMV kernel (IAM_QMM_GEMV_MAX_M
 // overrides: 0 sends every pass to the tensor-core kernel).

@@ -208,41 +208,35 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
   const int seg_tiles = (SG.rows + (sw ? 63 : 127)) / (sw ? 64 : 128);
   const bool fast = SG.packed[static_cast<size_t>(seg_tiles) * KB * kQpBlockBytes + tile] != 0;
   const int swz = qp_swz(g);  // rows 32 rp + 16 mt + g (+8) all share it
-  // offsets inside a stage's weight block: row R's word pair (k 64b + 16t ..)
-  // for the half's groups b = 2 beta + bb, and its (scale, bias) of those groups
-  int coff[2][2][2], soff[2][2];
+  // Stage offsets as a per-thread base plus compile-time terms (few live
+  // registers): row R = 32 rp + g + 16 mt + 8 h holds its word pair
+  // (k 64b + 16t ..) for the half's groups b = 2 beta + bb in chunk
+  // (2b + t/2) ^ swz, its (scale, bias) of those groups at 16 R + 8 beta.
+  const int cbase = L::kXBytes + (32 * rp + g) * 128 + (t & 1) * 8;
+  int cch[2];
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
+  for (int bb = 0; bb < 2; ++bb) cch[bb] = ((2 * (2 * beta + bb) + (t >> 1)) ^ swz) << 4;
+  const int sbbase = L::kXBytes + kQpCodeBytes + (32 * rp + g) * 16 + beta * 8;
+  // x: token row nt*8 + g, its 8 k at 64b + 16t + 8 delta in chunk (2t + delta) ^ g
+  const int xbase = 2 * beta * L::kXBox + g * 128;
+  int xch[2];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int R = 32 * rp + 16 * mt + g + 8 * h;
-#pragma unroll
-      for (int bb = 0; bb < 2; ++bb) {
-        const int b = 2 * beta + bb;
-        coff[mt][h][bb] = L::kXBytes + R * 128 + (((2 * b + (t >> 1)) ^ swz) << 4) + (t & 1) * 8;
-      }
-      soff[mt][h] = L::kXBytes + kQpCodeBytes + R * 16 + beta * 8;
-    }
-  // x: token row nt*8 + g, its 8 k at 64b + 16t + 8 delta
-  int xoff[2][2][NT];
+  for (int d = 0; d < 2; ++d) xch[d] = ((2 * t + d) ^ g) << 4;
   bool xon[NT];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    xon[nt] = nt * 8 + g < M;
+  for (int nt = 0; nt < NT; ++nt) xon[nt] = nt * 8 + g < M;
+
+  // one accumulator set per 64-k group of the half: four independent MMA
+  // chains a warp instead of two
+  float acc[2][2][NT][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
     for (int bb = 0; bb < 2; ++bb)
 #pragma unroll
-      for (int d = 0; d < 2; ++d)
-        xoff[bb][d][nt] = (2 * beta + bb) * L::kXBox + (nt * 8 + g) * 128 + (((2 * t + d) ^ g) << 4);
-  }
-
-  float acc[2][NT][4];
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
+        for (int e = 0; e < 4; ++e) acc[mt][bb][nt][e] = 0.f;
 
   // the block loop, compiled once per conversion form (a tile's scales pick it)
   auto blocks = [&](auto fast_tag) -> bool {
@@ -259,15 +253,16 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
         for (int d = 0; d < 2; ++d)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
-            xr[bb][d][nt] = xon[nt] ? lds128(stg + xoff[bb][d][nt]) : make_uint4(0u, 0u, 0u, 0u);
+            xr[bb][d][nt] = xon[nt] ? lds128(stg + xbase + bb * L::kXBox + nt * 1024 + xch[d])
+                                    : make_uint4(0u, 0u, 0u, 0u);
       uint2 cw[2][2][2], sb[2][2];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int bb = 0; bb < 2; ++bb) cw[mt][h][bb] = lds64(stg + coff[mt][h][bb]);
-          sb[mt][h] = lds64(stg + soff[mt][h]);
+          for (int bb = 0; bb < 2; ++bb) cw[mt][h][bb] = lds64(stg + cbase + mt * 2048 + h * 1024 + cch[bb]);
+          sb[mt][h] = lds64(stg + sbbase + mt * 256 + h * 128);
         }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty(s));
@@ -287,8 +282,8 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
             const uint32_t a23[4] = {v0[2], v1[2], v0[3], v1[3]};
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              mma_bf16_16816(acc[mt][nt], a01, xr[bb][d][nt].x, xr[bb][d][nt].y, acc[mt][nt]);
-              mma_bf16_16816(acc[mt][nt], a23, xr[bb][d][nt].z, xr[bb][d][nt].w, acc[mt][nt]);
+              mma_bf16_16816(acc[mt][bb][nt], a01, xr[bb][d][nt].x, xr[bb][d][nt].y, acc[mt][bb][nt]);
+              mma_bf16_16816(acc[mt][bb][nt], a23, xr[bb][d][nt].z, xr[bb][d][nt].w, acc[mt][bb][nt]);
             }
           }
         }
@@ -314,13 +309,14 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
     const int tok = nt * 8 + 2 * t + (e & 1);
     return row * TOK + tok;
   };
+  // in k order: group 2 beta, then 2 beta + 1, beta 0 before beta 1
   if (beta == 1) {
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) red[frag(mt, nt, e)] = acc[mt][nt][e];
+        for (int e = 0; e < 4; ++e) red[frag(mt, nt, e)] = acc[mt][0][nt][e] + acc[mt][1][nt][e];
   }
   named_bar_sync(1, kEpi);
   if (beta == 0) {
@@ -329,7 +325,8 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) red[frag(mt, nt, e)] += acc[mt][nt][e];
+        for (int e = 0; e < 4; ++e)
+          red[frag(mt, nt, e)] = (acc[mt][0][nt][e] + acc[mt][1][nt][e]) + red[frag(mt, nt, e)];
   }
   pdl_wait();  // outputs, residuals and the workspace follow the preceding kernel
   const bool good = !named_bar_or(1, kEpi, !ok || *abort_flag);
@@ -456,28 +453,21 @@ int gv_set_attr() {
   return IAM_OK;
 }
 
-// Split-K factor: spread tiles x k blocks over the SMs.  An SM streams about
-// 2.3 weight blocks a microsecond at the HBM roofline; a split costs its
-// partial stores, one arrival and the last CTA's sum.
+// Split-K factor.  A CTA streams its blocks at a rate bounded by latency
+// (about one 18 KiB block a microsecond), so the plan fills the GPU with two
+// resident CTAs an SM where the tile count allows: the smallest split that
+// gives about 1.8 CTAs an SM without a second wave, and never CTAs of fewer
+// than two blocks.  Matrices with at least 1.8 tiles an SM are not split.
 int gv_plan_ks(int tiles, int KB) {
   if (const char* v = std::getenv("IAM_QMM_GEMV_KS")) {
     const int k = std::atoi(v);
     if (k >= 1) return std::min(k, KB);
   }
-  const double r_sm = 2.3, c_split = 1.5;
-  double best = 1e30;
-  int bk = 1;
-  for (int ksp = 1; ksp <= std::min(KB, 32); ++ksp) {
-    const long ctas = static_cast<long>(tiles) * ksp;
-    const double per_sm = std::ceil(static_cast<double>(ctas) / g_gv_sms);
-    const double nb = std::ceil(static_cast<double>(KB) / ksp);
-    const double t = per_sm * nb / r_sm + (ksp > 1 ? c_split : 0.0);
-    if (t < best - 1e-9) {
-      best = t;
-      bk = ksp;
-    }
-  }
-  return bk;
+  const int slots = 2 * g_gv_sms;
+  int ks = (static_cast<int>(1.8 * g_gv_sms) + tiles - 1) / tiles;
+  if (static_cast<long>(tiles) * ks > slots) ks = slots / tiles;
+  ks = std::min(ks, std::max(1, KB / 2));
+  return std::max(ks, 1);
 }
 
 template <int NT>
@@ -503,7 +493,7 @@ int gv_launch(const QmmGvArgs& ga, int ks, cudaStream_t st, bool pdl) {
 int qmm_gemv_max_m() {
   // read on every call (host side, once per matmul launch or graph capture)
   if (const char* e = std::getenv("IAM_QMM_GEMV_MAX_M")) return std::max(0, std::min(std::atoi(e), kGemvMaxM));
-  return kGemvMaxM;
+  return kGemvDefaultMaxM;
 }
 
 int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap) {

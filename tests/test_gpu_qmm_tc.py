@@ -1,9 +1,9 @@
 """The W4A16 matmul on packed weights through the C ABI: the packed weight
 layout byte for byte against a numpy restatement, and the matmul against the
 oracle restatement of MLX's qmm -- on the register-dequant GEMV kernel
-(mma.sync, passes of up to 16 tokens) and on the tensor-core kernel (tcgen05,
-weights dequantized into tensor memory; wider passes, or every pass with
-IAM_QMM_GEMV_MAX_M=0).
+(mma.sync; passes of up to 8 tokens by default, 16 with IAM_QMM_GEMV_MAX_M=16)
+and on the tensor-core kernel (tcgen05, weights dequantized into tensor
+memory; wider passes, or every pass with IAM_QMM_GEMV_MAX_M=0).
 
 Tolerance as for iam_qmm_affine4: both sides multiply x with the bf16 weights
 bf16(q * scale + bias); only the fp32 accumulation order differs, so relative
@@ -106,12 +106,15 @@ def test_pack_layout_matches_restatement():
     assert np.array_equal(got, ref)
 
 
-@pytest.fixture(params=["default", "tensor_core"])
+@pytest.fixture(params=["default", "tensor_core", "gemv16"])
 def kernel(request, monkeypatch):
-    """The library's kernel choice (GEMV up to 16 tokens), or the tensor-core
-    kernel at every width."""
+    """The library's kernel choice (GEMV up to 8 tokens), the tensor-core
+    kernel at every width, or the GEMV kernel up to 16 tokens (its 16-token
+    tile)."""
     if request.param == "tensor_core":
         monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "0")
+    elif request.param == "gemv16":
+        monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "16")
     return request.param
 
 
