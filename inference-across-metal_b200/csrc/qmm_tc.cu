@@ -54,7 +54,6 @@ constexpr int kTcThreads = 32 * (2 + kTcDqWarps);
 constexpr int kTcASlots = 3;                         // TMEM A slots of one 256-k block (128 columns)
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcDCol = 128 * kTcASlots;        // accumulator: NN (<= 64) columns
-constexpr int kTcMaxSplit = 8;                       // k splits of a tile: one cluster (portable size)
 
 constexpr uint32_t kMagic = 0x43004300u;
 constexpr uint32_t kNibMask = 0x000F000Fu;
@@ -94,17 +93,10 @@ __device__ __forceinline__ void dequant_group_fast(const uint4& c0, const uint4&
   }
 }
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// the float at this CTA's shared address of p, in the shared memory of
-// cluster CTA `rank`
-__device__ __forceinline__ float ld_peer(const float* p, uint32_t rank) {
-  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p)), ra;
-  float v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-  return v;
+__device__ __forceinline__ float4 ld_cg_f4(const float* p) {
+  float4 r;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(p));
+  return r;
 }
 
 // Cursor over an N-stage ring: stage index and the parity of its current lap
@@ -182,6 +174,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
   unsigned char* tail = smem + L::kBarOff + L::kNumBars * 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tail);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 8);
+  int* last_flag = reinterpret_cast<int*>(tail + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bx = blockIdx.x;
@@ -293,11 +286,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
       for (int i = max(0, ix - XS); i < ix; ++i)
         if (!mbar_wait(xfull(i % XS), (i / XS) & 1)) give_up();
     }
-    __syncwarp();
-    if (KS > 1) {  // the cluster barriers of the split-K epilogue
-      cluster_sync_all();
-      cluster_sync_all();
-    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     // The warp runs the loop converged and one elected lane issues.  Each
@@ -335,10 +323,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     __syncwarp();
     // every MMA of this CTA has completed once dfull flips
     if (!__all_sync(0xffffffffu, mbar_wait(dfull, 0))) give_up();
-    if (KS > 1) {  // the cluster barriers of the split-K epilogue
-      cluster_sync_all();
-      cluster_sync_all();
-    }
   } else {
     // ------------------------------------------------------------ dequantizers
     const int q = warp & 3, h = (warp - 2) >> 2;  // h: 64-k group of each block
@@ -416,85 +400,48 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     pdl_wait();
     // one verdict for all epilogue threads (their named barriers below)
     const bool ok = !named_bar_or(1, 32 * kTcDqWarps, !have || *abort_flag);
+    bool last = true;
     if (KS > 1) {
-      // Split-K: the k splits of a tile are one thread-block cluster (cluster
-      // rank = split).  Each CTA puts its partial [128 rows][NN tokens] in its
-      // (idle) activation ring; after a cluster barrier it finishes a slice
-      // of the tile's rows from all splits' partials, read through
-      // distributed shared memory and summed in split order (the same bits
-      // whichever CTA sums them); a second barrier keeps every partial alive
-      // until the peers have read it.
-      float* red = reinterpret_cast<float*>(smem);
+      // split-K: each CTA stores its partial in its own slice [ks][row][token];
+      // the last CTA of the tile sums the slices in ks order (reproducible bits)
+      float* base = A.ws + static_cast<size_t>(bx) * KS * kQpRows * NN + static_cast<size_t>(row) * NN + tok0;
+      if (ok) {
+        float* mine = base + static_cast<size_t>(ks) * kQpRows * NN;
 #pragma unroll
-      for (int c4 = 0; c4 < EC / 4; ++c4)
-        *reinterpret_cast<float4*>(red + row * NN + tok0 + 4 * c4) =
-            make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
-      cluster_sync_all();
-      auto sum_rt = [&](int r, int tok) -> float {
-        float a = 0.f;
-        for (int j = 0; j < KS; ++j) a += ld_peer(&red[r * NN + tok], static_cast<uint32_t>(j));
-        return a;
-      };
-      const int td = threadIdx.x - 64;  // 0 .. 511
-      constexpr int kDq = 32 * kTcDqWarps;
-      const int mode = S.mode;
-      const int M = A.M;
-      if (ok && mode == EPI_ARGMAX) {
-        if (ks == 0) {  // split 0 alone: the best key of each token over the tile's rows
-          unsigned long long* kbuf = reinterpret_cast<unsigned long long*>(smem + kQpRows * NN * 4);  // [4][NN]
-          const int r = td & 127, tg = td >> 7;
-          const int grow = tile * kQpRows + r;
-          for (int tok = tg; tok < NN; tok += 4) {
-            unsigned long long k = 0ull;
-            if (grow < S.rows) k = argmax_key(round_bf(sum_rt(r, tok)), static_cast<uint32_t>(S.col_base + grow));
+        for (int c4 = 0; c4 < EC / 4; ++c4)
+          *reinterpret_cast<float4*>(mine + 4 * c4) = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+      }
+      // The barrier orders every thread's partial before one GPU-scope
+      // acquire-release arrival (cumulative, so it publishes the whole CTA's
+      // partial and, for the last arrival, acquires the others').
+      named_bar_sync(1, 32 * kTcDqWarps);
+      if (threadIdx.x == 64) {
+        int* ctr = A.counters + bx;
+        int prev;
+        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
+        const int l = prev == KS - 1;
+        if (l) *ctr = 0;
+        *last_flag = l;
+      }
+      named_bar_sync(1, 32 * kTcDqWarps);
+      last = *last_flag != 0;
+      if (last) {
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
-              k = other > k ? other : k;
-            }
-            if (lane == 0) kbuf[(r >> 5) * NN + tok] = k;
-          }
-          named_bar_sync(1, kDq);
-          if (td < NN && td < M) {
-            unsigned long long k = kbuf[td];
+        for (int e = 0; e < EC; ++e) v[e] = 0.f;
+        for (int j = 0; j < KS; ++j) {
+          const float* p = base + static_cast<size_t>(j) * kQpRows * NN;
 #pragma unroll
-            for (int qq = 1; qq < 4; ++qq) k = kbuf[qq * NN + td] > k ? kbuf[qq * NN + td] : k;
-            S.keys[static_cast<size_t>(tile) * S.key_ld + td] = k;
-          }
-        }
-      } else if (ok && mode == EPI_SWIGLU) {
-        const int f0 = (ks * 64) / KS, nf = ((ks + 1) * 64) / KS - f0;
-        uint16_t* const out = S.out;
-        const size_t ldo = static_cast<size_t>(S.ldo);
-        for (int idx = td; idx < nf * M; idx += kDq) {
-          const int tok = idx / nf, f = f0 + idx % nf;
-          const int feat = tile * 64 + f;
-          if (feat < S.rows)
-            out[tok * ldo + feat] = f2bf(silu_f(round_bf(sum_rt(f, tok))) * round_bf(sum_rt(f + 64, tok)));
-        }
-      } else if (ok) {
-        const int r0 = (ks * kQpRows) / KS, nr = ((ks + 1) * kQpRows) / KS - r0;
-        uint16_t* const out = S.out;
-        float* const out32 = S.out32;
-        const uint16_t* const resid = S.resid;
-        const size_t ldo = static_cast<size_t>(S.ldo), ldr = static_cast<size_t>(S.ldr);
-        for (int idx = td; idx < nr * M; idx += kDq) {
-          const int tok = idx / nr, r = r0 + idx % nr;
-          const int grow = tile * kQpRows + r;
-          if (grow >= S.rows) continue;
-          const float a = sum_rt(r, tok);
-          const size_t o = tok * ldo + grow;
-          if (mode == EPI_F32) {
-            out32[o] = a;
-          } else if (mode == EPI_RESID) {
-            out[o] = f2bf(bf2f(resid[tok * ldr + grow]) + round_bf(a));
-          } else {
-            out[o] = f2bf(a);
+          for (int c4 = 0; c4 < EC / 4; ++c4) {
+            const float4 t = ld_cg_f4(p + 4 * c4);
+            v[4 * c4] += t.x;
+            v[4 * c4 + 1] += t.y;
+            v[4 * c4 + 2] += t.z;
+            v[4 * c4 + 3] += t.w;
           }
         }
       }
-      cluster_sync_all();
-    } else if (ok) {
+    }
+    if (last && ok) {
       const int mode = S.mode;
       if (mode == EPI_SWIGLU) {
         // rows 0-63 gate, 64-127 up of features tile*64 + (row & 63)
@@ -658,13 +605,13 @@ int tc_occupancy() {
 int tc_plan_ks(int tiles, int KB, int occ) {
   if (const char* v = std::getenv("IAM_QMM_TC_KS")) {
     const int k = std::atoi(v);
-    if (k >= 1) return std::min({k, KB, kTcMaxSplit});
+    if (k >= 1) return std::min(k, KB);
   }
   const double r_sm = 2.6, r_cta = 2.6, c0 = 2.0, c1 = 1.0;
   const long slots = static_cast<long>(g_tc_sms) * occ;
   double best = 1e30;
   int bk = 1;
-  for (int ksp = 1; ksp <= std::min(KB, kTcMaxSplit); ++ksp) {
+  for (int ksp = 1; ksp <= std::min(KB, 32); ++ksp) {
     const long ctas = static_cast<long>(tiles) * ksp;
     const long waves = (ctas + slots - 1) / slots;
     const double per_sm = std::ceil(static_cast<double>(std::min(ctas, slots)) / g_tc_sms);
@@ -721,22 +668,11 @@ static int tc_launch(const QmmTcArgs& ta, int ks, cudaStream_t st, bool pdl) {
   cfg.blockDim = dim3(kTcThreads, 1, 1);
   cfg.dynamicSmemBytes = TcLayout<NN>::kSmem;
   cfg.stream = st;
-  // the k splits of a tile form one cluster (their partials meet in
-  // distributed shared memory)
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  attr[na].id = cudaLaunchAttributeClusterDimension;
-  attr[na].val.clusterDim.x = 1;
-  attr[na].val.clusterDim.y = 1;
-  attr[na].val.clusterDim.z = static_cast<unsigned>(ks);
-  ++na;
-  if (pdl) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = na;
+  cfg.numAttrs = pdl ? 1 : 0;
   IAM_CUDA(cudaLaunchKernelEx(&cfg, qmm_tc_kernel<NN>, ta));
   return IAM_OK;
 }
@@ -767,9 +703,22 @@ int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_
   const int NN = a.M <= 16 ? 16 : a.M <= 32 ? 32 : 64;
   const int KB = qp_kblocks(a.K);
   const int occ = NN == 16 ? tc_occupancy<16>() : NN == 32 ? tc_occupancy<32>() : tc_occupancy<64>();
-  const int ks = tc_plan_ks(cta, KB, occ);
-  (void)ws_floats_cap;
-  (void)ws_ctr_cap;  // split-K partials meet in distributed shared memory: no workspace
+  int ks = tc_plan_ks(cta, KB, occ);
+  if (ks > 1 && a.ws) {  // a caller's workspace bounds the split
+    const size_t per = static_cast<size_t>(cta) * kQpRows * NN;
+    ks = static_cast<int>(std::min<size_t>(ks, ws_floats_cap / per));
+    if (static_cast<size_t>(cta) > ws_ctr_cap) ks = 1;
+    ks = std::max(ks, 1);
+  }
+  if (ks > 1) {
+    const size_t nf = static_cast<size_t>(cta) * ks * kQpRows * NN, nc = static_cast<size_t>(cta);
+    if (!a.ws) {
+      const int r = qmm_op_workspace(1, nf, nc, st, &a.ws, &a.counters);
+      if (r != IAM_OK) return r;
+    } else {
+      IAM_CHECK(nf <= ws_floats_cap && nc <= ws_ctr_cap, "qmm: split-K workspace too small");
+    }
+  }
   QmmTcArgs ta;
   std::memset(&ta, 0, sizeof(ta));
   ta.a = a;
