@@ -26,12 +26,10 @@
 //    in A and B (lane t's physical pairs take its fragment slots 2t and
 //    2t+8), which leaves the sums unchanged;
 //  * the two k halves are added through shared memory; with the k range split
-//    over CTAs (at most 8) the splits of a tile form one thread-block
-//    cluster, and each CTA finishes a slice of the tile's rows from all the
-//    splits' partials, read through distributed shared memory and summed in
-//    split order -- bitwise reproducible, no global workspace, no atomics;
-//    then the fused epilogue (store, residual, SwiGLU, argmax keys, fp32
-//    partials).
+//    over CTAs each stores its fp32 partial and the last CTA of the tile (one
+//    acquire-release counter) sums them in split order -- bitwise
+//    reproducible; then the fused epilogue (store, residual, SwiGLU, argmax
+//    keys, fp32 partials).
 // Every mbarrier wait is bounded; a wait that gives up records IAM_ETIMEOUT,
 // and the producer drains its copies before the CTA exits.
 #include <algorithm>
@@ -50,7 +48,6 @@ namespace {
 constexpr int kGvWarps = 8;                          // consumer warps
 constexpr int kGvThreads = 32 * (kGvWarps + 1);      // + the producer warp
 constexpr int kGvStages = 4;
-constexpr int kGvMaxSplit = 8;                       // k splits of a tile: one cluster (portable size)
 
 template <int NT>
 struct GvLayout {
@@ -62,7 +59,7 @@ struct GvLayout {
   static_assert(kStage % 1024 == 0, "stages keep the activation boxes 1 KiB aligned");
   static constexpr int kBarOff = kGvStages * kStage;
   static constexpr int kNumBars = 2 * kGvStages;           // full[S], empty[S]
-  // barriers, then the abort flag (64 bytes reserved), then this CTA's segment
+  // barriers, then abort / last flags (64 bytes), then this CTA's segment
   static constexpr int kSmem = kBarOff + kNumBars * 8 + 64 + 128 + 1024;  // + alignment slack
   // after the block loop the ring holds the tile's sums [128][kTok] fp32 and
   // the argmax keys [4][kTok]
@@ -98,18 +95,10 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t s2, uint32_t b
 
 __device__ __forceinline__ uint2 lds64(const unsigned char* p) { return *reinterpret_cast<const uint2*>(p); }
 __device__ __forceinline__ uint4 lds128(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// the float at this CTA's shared address of p, in the shared memory of
-// cluster CTA `rank`
-__device__ __forceinline__ float ld_peer(const float* p, uint32_t rank) {
-  uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p)), ra;
-  float v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-  return v;
+__device__ __forceinline__ float4 ld_cg_f4(const float* p) {
+  float4 r;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(p));
+  return r;
 }
 
 struct QmmGvArgs {
@@ -131,6 +120,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
   auto empty = [&](int s) { return bar0 + 8u * (S + s); };
   unsigned char* tail = smem + L::kBarOff + L::kNumBars * 8;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tail);
+  int* last_flag = reinterpret_cast<int*>(tail + 8);
   QmmSeg* seg_copy = reinterpret_cast<QmmSeg*>(tail + 64);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -207,13 +197,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
       for (int i = max(0, issued - S); i < issued; ++i)
         if (!mbar_wait(full(i % S), (i / S) & 1)) give_up();
     }
-    __syncwarp();
-    // the producer warp takes part only in the cluster barriers below
-    if (KS > 1) {
-      cluster_sync_all();
-      cluster_sync_all();
-    }
-    return;
+    return;  // the producer takes no part in the epilogue
   }
 
   // -------------------------------------------------------------- consumers
@@ -344,82 +328,116 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
         for (int e = 0; e < 4; ++e)
           red[frag(mt, nt, e)] = (acc[mt][0][nt][e] + acc[mt][1][nt][e]) + red[frag(mt, nt, e)];
   }
-  pdl_wait();  // outputs and residuals follow the preceding kernel
+  pdl_wait();  // outputs, residuals and the workspace follow the preceding kernel
   const bool good = !named_bar_or(1, kEpi, !ok || *abort_flag);
-  // The k splits of a tile run as one thread-block cluster (cluster rank =
-  // split): after one cluster barrier every CTA finishes a slice of the
-  // tile's rows, summing the splits' partials from distributed shared memory
-  // in split order -- the same bits whichever CTA sums them -- and a second
-  // barrier keeps each CTA's partial alive until its peers have read it.
-  if (KS > 1) cluster_sync_all();
-  auto sum_rt = [&](int r, int tok) -> float {
-    if (KS == 1) return red[r * TOK + tok];
-    float v = 0.f;
-    for (int j = 0; j < KS; ++j) v += ld_peer(&red[r * TOK + tok], static_cast<uint32_t>(j));
-    return v;
-  };
-  if (good) {
-    const int mode = SG.mode;
-    if (mode == EPI_ARGMAX) {
-      // per token: the best (value, first index) key over the tile's rows
-      // (split 0 alone); warp w holds rows 32 (w & 3) .. +31 of tokens
-      // (w >> 2) + 2j
-      if (ks == 0) {
-        const int row = ct & 127, tpar = ct >> 7;
-        const int grow = tile * kQpRows + row;
-        for (int tok = tpar; tok < TOK; tok += 2) {
-          unsigned long long k = 0ull;
-          if (grow < SG.rows) k = argmax_key(round_bf(sum_rt(row, tok)), static_cast<uint32_t>(SG.col_base + grow));
+  // thread ct: row ct & 127, tokens (ct >> 7) + 2j
+  const int row = ct & 127, tpar = ct >> 7;
+  constexpr int TPT = TOK / 2;  // tokens a thread
+  float v[TPT];
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
-            k = other > k ? other : k;
-          }
-          if (lane == 0) kbuf[(warp & 3) * TOK + tok] = k;
-        }
-        named_bar_sync(2, kEpi);
-        if (ct < TOK && ct < M) {
-          unsigned long long k = kbuf[ct];
+  for (int j = 0; j < TPT; ++j) v[j] = red[row * TOK + tpar + 2 * j];
+  bool last = true;
+  if (KS > 1) {
+    float* base = A.ws + static_cast<size_t>(bx) * KS * kQpRows * TOK + static_cast<size_t>(row) * TOK;
+    if (good) {
+      float* mine = base + static_cast<size_t>(ks) * kQpRows * TOK;
 #pragma unroll
-          for (int qq = 1; qq < 4; ++qq) k = kbuf[qq * TOK + ct] > k ? kbuf[qq * TOK + ct] : k;
-          SG.keys[static_cast<size_t>(tile) * SG.key_ld + ct] = k;
-        }
-      }
-    } else if (mode == EPI_SWIGLU) {
-      // tile rows 0-63 gate, 64-127 up of features tile*64 + f; this split
-      // finishes features [f0, f1)
-      const int f0 = (ks * 64) / KS, nf = ((ks + 1) * 64) / KS - f0;
-      uint16_t* const out = SG.out;
-      const size_t ldo = static_cast<size_t>(SG.ldo);
-      for (int idx = ct; idx < nf * M; idx += kEpi) {
-        const int tok = idx / nf, f = f0 + idx % nf;
-        const int feat = tile * 64 + f;
-        if (feat < SG.rows) out[tok * ldo + feat] = f2bf(silu_f(round_bf(sum_rt(f, tok))) * round_bf(sum_rt(f + 64, tok)));
-      }
-    } else {
-      // this split finishes rows [r0, r0 + nr) of the tile
-      const int r0 = (ks * kQpRows) / KS, nr = ((ks + 1) * kQpRows) / KS - r0;
-      uint16_t* const out = SG.out;
-      float* const out32 = SG.out32;
-      const uint16_t* const resid = SG.resid;
-      const size_t ldo = static_cast<size_t>(SG.ldo), ldr = static_cast<size_t>(SG.ldr);
-      for (int idx = ct; idx < nr * M; idx += kEpi) {
-        const int tok = idx / nr, r = r0 + idx % nr;
-        const int grow = tile * kQpRows + r;
-        if (grow >= SG.rows) continue;
-        const float v = sum_rt(r, tok);
-        const size_t o = tok * ldo + grow;
-        if (mode == EPI_F32) {
-          out32[o] = v;
-        } else if (mode == EPI_RESID) {
-          out[o] = f2bf(bf2f(resid[tok * ldr + grow]) + round_bf(v));
-        } else {
-          out[o] = f2bf(v);
+      for (int j = 0; j < TPT; ++j) mine[tpar + 2 * j] = v[j];
+    }
+    named_bar_sync(1, kEpi);
+    if (ct == 0) {
+      int* ctr = A.counters + bx;
+      int prev;
+      asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
+      const int l = prev == KS - 1;
+      if (l) *ctr = 0;
+      *last_flag = l;
+    }
+    named_bar_sync(1, kEpi);
+    last = *last_flag != 0;
+    if (last) {
+      // every split's partial, in split order (reproducible bits)
+#pragma unroll
+      for (int j = 0; j < TPT; ++j) v[j] = 0.f;
+      for (int q = 0; q < KS; ++q) {
+        const float* p = base + static_cast<size_t>(q) * kQpRows * TOK;
+        // the row's TOK floats; this thread's are tokens tpar, tpar + 2, ...
+#pragma unroll
+        for (int c4 = 0; c4 < TOK / 4; ++c4) {
+          const float4 f = ld_cg_f4(p + 4 * c4);
+          const float fv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if ((4 * c4 + e) % 2 == tpar) v[(4 * c4 + e) / 2] += fv[e];
         }
       }
     }
   }
-  if (KS > 1) cluster_sync_all();
+  if (last && good) {
+    const int mode = SG.mode;
+    if (mode == EPI_SWIGLU || mode == EPI_ARGMAX) {
+      named_bar_sync(2, kEpi);  // every thread has read red
+#pragma unroll
+      for (int j = 0; j < TPT; ++j) red[row * TOK + tpar + 2 * j] = v[j];
+      named_bar_sync(2, kEpi);
+    }
+    if (mode == EPI_SWIGLU) {
+      // rows 0-63 gate, 64-127 up of features tile*64 + (row & 63)
+      const int f = tile * 64 + row;
+      uint16_t* const out = SG.out;
+      const size_t ldo = static_cast<size_t>(SG.ldo);
+      if (row < 64 && f < SG.rows) {
+#pragma unroll
+        for (int j = 0; j < TPT; ++j) {
+          const int tok = tpar + 2 * j;
+          if (tok < M) out[tok * ldo + f] = f2bf(silu_f(round_bf(v[j])) * round_bf(red[(row + 64) * TOK + tok]));
+        }
+      }
+    } else if (mode == EPI_ARGMAX) {
+      // per token: the best (value, first index) key over the tile's rows;
+      // warp w holds rows 32 (w & 3) .. +31 of tokens (w >> 2) + 2j
+      const int grow = tile * kQpRows + row;
+#pragma unroll
+      for (int j = 0; j < TPT; ++j) {
+        unsigned long long k = 0ull;
+        if (grow < SG.rows) k = argmax_key(round_bf(v[j]), static_cast<uint32_t>(SG.col_base + grow));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
+          k = other > k ? other : k;
+        }
+        if (lane == 0) kbuf[(warp & 3) * TOK + tpar + 2 * j] = k;
+      }
+      named_bar_sync(2, kEpi);
+      if (ct < TOK && ct < M) {
+        unsigned long long k = kbuf[ct];
+#pragma unroll
+        for (int qq = 1; qq < 4; ++qq) k = kbuf[qq * TOK + ct] > k ? kbuf[qq * TOK + ct] : k;
+        SG.keys[static_cast<size_t>(tile) * SG.key_ld + ct] = k;
+      }
+    } else {
+      const int grow = tile * kQpRows + row;
+      uint16_t* const out = SG.out;
+      float* const out32 = SG.out32;
+      const uint16_t* const resid = SG.resid;
+      const size_t ldo = static_cast<size_t>(SG.ldo), ldr = static_cast<size_t>(SG.ldr);
+      if (grow < SG.rows) {
+#pragma unroll
+        for (int j = 0; j < TPT; ++j) {
+          const int tok = tpar + 2 * j;
+          if (tok >= M) continue;
+          const size_t o = tok * ldo + grow;
+          if (mode == EPI_F32) {
+            out32[o] = v[j];
+          } else if (mode == EPI_RESID) {
+            out[o] = f2bf(bf2f(resid[tok * ldr + grow]) + round_bf(v[j]));
+          } else {
+            out[o] = f2bf(v[j]);
+          }
+        }
+      }
+    }
+  }
 }
 
 int g_gv_sms = 0;
@@ -443,13 +461,13 @@ int gv_set_attr() {
 int gv_plan_ks(int tiles, int KB) {
   if (const char* v = std::getenv("IAM_QMM_GEMV_KS")) {
     const int k = std::atoi(v);
-    if (k >= 1) return std::min({k, KB, kGvMaxSplit});
+    if (k >= 1) return std::min(k, KB);
   }
   const int slots = 2 * g_gv_sms;
   int ks = (static_cast<int>(1.8 * g_gv_sms) + tiles - 1) / tiles;
   if (static_cast<long>(tiles) * ks > slots) ks = slots / tiles;
   ks = std::min(ks, std::max(1, KB / 2));
-  return std::max(1, std::min(ks, kGvMaxSplit));
+  return std::max(ks, 1);
 }
 
 template <int NT>
@@ -461,22 +479,11 @@ int gv_launch(const QmmGvArgs& ga, int ks, cudaStream_t st, bool pdl) {
   cfg.blockDim = dim3(kGvThreads, 1, 1);
   cfg.dynamicSmemBytes = GvLayout<NT>::kSmem;
   cfg.stream = st;
-  // the k splits of a tile form one cluster (their partials meet in
-  // distributed shared memory)
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  attr[na].id = cudaLaunchAttributeClusterDimension;
-  attr[na].val.clusterDim.x = 1;
-  attr[na].val.clusterDim.y = 1;
-  attr[na].val.clusterDim.z = static_cast<unsigned>(ks);
-  ++na;
-  if (pdl) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = na;
+  cfg.numAttrs = pdl ? 1 : 0;
   IAM_CUDA(cudaLaunchKernelEx(&cfg, qmm_gemv_kernel<NT>, ga));
   return IAM_OK;
 }
@@ -515,9 +522,22 @@ int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, siz
   const int NT = a.M <= 8 ? 1 : 2;
   const int TOK = 8 * NT;
   const int KB = qp_kblocks(a.K);
-  const int ks = gv_plan_ks(cta, KB);
-  (void)ws_floats_cap;
-  (void)ws_ctr_cap;  // split-K partials meet in distributed shared memory: no workspace
+  int ks = gv_plan_ks(cta, KB);
+  if (ks > 1 && a.ws) {  // a caller's workspace bounds the split
+    const size_t per = static_cast<size_t>(cta) * kQpRows * TOK;
+    ks = static_cast<int>(std::min<size_t>(ks, ws_floats_cap / per));
+    if (static_cast<size_t>(cta) > ws_ctr_cap) ks = 1;
+    ks = std::max(ks, 1);
+  }
+  if (ks > 1) {
+    const size_t nf = static_cast<size_t>(cta) * ks * kQpRows * TOK, nc = static_cast<size_t>(cta);
+    if (!a.ws) {
+      const int r = qmm_op_workspace(1, nf, nc, st, &a.ws, &a.counters);
+      if (r != IAM_OK) return r;
+    } else {
+      IAM_CHECK(nf <= ws_floats_cap && nc <= ws_ctr_cap, "qmm: split-K workspace too small");
+    }
+  }
   QmmGvArgs ga;
   std::memset(&ga, 0, sizeof(ga));
   ga.a = a;
