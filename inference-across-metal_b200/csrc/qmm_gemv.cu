@@ -45,13 +45,16 @@
 namespace iam {
 namespace {
 
-constexpr int kGvWarps = 8;                          // consumer warps
-constexpr int kGvThreads = 32 * (kGvWarps + 1);      // + the producer warp
 constexpr int kGvStages = 4;
+// QW: the number of consumer warps sharing one 32-row pair of a block, each
+// taking 4 / QW of its four 64-k groups; 4 QW consumer warps + 1 producer.
+__host__ __device__ constexpr int gv_warps(int QW) { return 4 * QW; }
+__host__ __device__ constexpr int gv_threads(int QW) { return 32 * (gv_warps(QW) + 1); }
 
-template <int NT>
+template <int NT, int QW = 4>
 struct GvLayout {
   static_assert(NT == 1 || NT == 2, "8 or 16 tokens a pass");
+  static_assert(QW == 2 || QW == 4, "2 or 4 warps on a row pair");
   static constexpr int kTok = 8 * NT;
   static constexpr int kXBox = kTok * 128;                 // one [kTok x 64 k] box
   static constexpr int kXBytes = 4 * kXBox;                // the block's 256 k of activations
@@ -61,10 +64,11 @@ struct GvLayout {
   static constexpr int kNumBars = 2 * kGvStages;           // full[S], empty[S]
   // barriers, then abort / last flags (64 bytes), then this CTA's segment
   static constexpr int kSmem = kBarOff + kNumBars * 8 + 64 + 128 + 1024;  // + alignment slack
-  // after the block loop the ring holds the tile's sums [128][kTok] fp32 and
-  // the argmax keys [4][kTok]
+  // after the block loop the ring holds the k parts' partials [QW][128][kTok]
+  // fp32, the tile's sums [128][kTok] and the argmax keys [4][kTok]
   static constexpr int kRedBytes = 128 * kTok * 4;
-  static_assert(kRedBytes + 4 * kTok * 8 <= kBarOff, "epilogue buffers fit in the ring");
+  static constexpr int kPartOff = kRedBytes + 4 * kTok * 8;
+  static_assert(kPartOff + QW * kRedBytes <= kBarOff, "epilogue buffers fit in the ring");
   static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
   static_assert(sizeof(QmmSeg) <= 128, "segment copy");
 };
@@ -106,10 +110,12 @@ struct QmmGvArgs {
   QmmArgs a;
 };
 
-template <int NT>
-__global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_constant__ QmmGvArgs T) {
-  using L = GvLayout<NT>;
+template <int NT, int QW>
+__global__ void __launch_bounds__(gv_threads(QW), 2) qmm_gemv_kernel(const __grid_constant__ QmmGvArgs T) {
+  using L = GvLayout<NT, QW>;
   constexpr int S = kGvStages, TOK = L::kTok;
+  constexpr int kGvWarps = gv_warps(QW);
+  constexpr int GPW = 4 / QW;  // 64-k groups of a block a warp converts
   const QmmArgs& A = T.a;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char* smem =
@@ -201,7 +207,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
   }
 
   // -------------------------------------------------------------- consumers
-  const int rp = warp >> 1, beta = warp & 1;
+  const int rp = warp / QW, qp = warp % QW;  // row pair, k part (groups GPW qp .. +GPW-1)
   const int g = lane >> 2, t = lane & 3;
   const int M = A.M;
   const bool sw = SG.mode == EPI_SWIGLU;
@@ -210,15 +216,15 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
   const int swz = qp_swz(g);  // rows 32 rp + 16 mt + g (+8) all share it
   // Stage offsets as a per-thread base plus compile-time terms (few live
   // registers): row R = 32 rp + g + 16 mt + 8 h holds its word pair
-  // (k 64b + 16t ..) for the half's groups b = 2 beta + bb in chunk
-  // (2b + t/2) ^ swz, its (scale, bias) of those groups at 16 R + 8 beta.
+  // (k 64b + 16t ..) of group b = GPW qp + bb in chunk (2b + t/2) ^ swz, and
+  // its (scale, bias) of that group at 16 R + 4 b.
   const int cbase = L::kXBytes + (32 * rp + g) * 128 + (t & 1) * 8;
-  int cch[2];
+  int cch[GPW];
 #pragma unroll
-  for (int bb = 0; bb < 2; ++bb) cch[bb] = ((2 * (2 * beta + bb) + (t >> 1)) ^ swz) << 4;
-  const int sbbase = L::kXBytes + kQpCodeBytes + (32 * rp + g) * 16 + beta * 8;
+  for (int bb = 0; bb < GPW; ++bb) cch[bb] = ((2 * (GPW * qp + bb) + (t >> 1)) ^ swz) << 4;
+  const int sbbase = L::kXBytes + kQpCodeBytes + (32 * rp + g) * 16 + GPW * qp * 4;
   // x: token row nt*8 + g, its 8 k at 64b + 16t + 8 delta in chunk (2t + delta) ^ g
-  const int xbase = 2 * beta * L::kXBox + g * 128;
+  const int xbase = GPW * qp * L::kXBox + g * 128;
   int xch[2];
 #pragma unroll
   for (int d = 0; d < 2; ++d) xch[d] = ((2 * t + d) ^ g) << 4;
@@ -226,13 +232,12 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) xon[nt] = nt * 8 + g < M;
 
-  // one accumulator set per 64-k group of the half: four independent MMA
-  // chains a warp instead of two
-  float acc[2][2][NT][4];
+  // one accumulator set per 64-k group of the warp: independent MMA chains
+  float acc[2][GPW][NT][4];
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int bb = 0; bb < 2; ++bb)
+    for (int bb = 0; bb < GPW; ++bb)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -246,31 +251,38 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
     for (int i = 0; i < nkb; ++i) {
       if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(full(s), phase, abort_flag, lim))) return false;
       const unsigned char* stg = smem + s * L::kStage;
-      uint4 xr[2][2][NT];
+      uint4 xr[GPW][2][NT];
 #pragma unroll
-      for (int bb = 0; bb < 2; ++bb)
+      for (int bb = 0; bb < GPW; ++bb)
 #pragma unroll
         for (int d = 0; d < 2; ++d)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
             xr[bb][d][nt] = xon[nt] ? lds128(stg + xbase + bb * L::kXBox + nt * 1024 + xch[d])
                                     : make_uint4(0u, 0u, 0u, 0u);
-      uint2 cw[2][2][2], sb[2][2];
+      uint2 cw[2][2][GPW];
+      uint32_t sb[2][2][GPW];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int bb = 0; bb < 2; ++bb) cw[mt][h][bb] = lds64(stg + cbase + mt * 2048 + h * 1024 + cch[bb]);
-          sb[mt][h] = lds64(stg + sbbase + mt * 256 + h * 128);
+          for (int bb = 0; bb < GPW; ++bb) cw[mt][h][bb] = lds64(stg + cbase + mt * 2048 + h * 1024 + cch[bb]);
+          if constexpr (GPW == 2) {
+            const uint2 p = lds64(stg + sbbase + mt * 256 + h * 128);
+            sb[mt][h][0] = p.x;
+            sb[mt][h][GPW - 1] = p.y;
+          } else {
+            sb[mt][h][0] = *reinterpret_cast<const uint32_t*>(stg + sbbase + mt * 256 + h * 128);
+          }
         }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty(s));
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int bb = 0; bb < 2; ++bb) {
-          const uint32_t sb0 = bb ? sb[mt][0].y : sb[mt][0].x, sb1 = bb ? sb[mt][1].y : sb[mt][1].x;
+        for (int bb = 0; bb < GPW; ++bb) {
+          const uint32_t sb0 = sb[mt][0][bb], sb1 = sb[mt][1][bb];
           const uint32_t s20 = prmt(sb0, sb0, 0x1010u), b20 = prmt(sb0, sb0, 0x3232u);
           const uint32_t s21 = prmt(sb1, sb1, 0x1010u), b21 = prmt(sb1, sb1, 0x3232u);
 #pragma unroll
@@ -299,50 +311,46 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
 
   // ------------------------------------------------------------ epilogue
   constexpr int kEpi = 32 * kGvWarps;
-  const int ct = threadIdx.x;  // 0 .. 255
+  const int ct = threadIdx.x;  // 0 .. kEpi - 1
   float* red = reinterpret_cast<float*>(smem);  // [128][TOK], over the idle ring
   unsigned long long* kbuf = reinterpret_cast<unsigned long long*>(smem + L::kRedBytes);  // [4][TOK]
+  float* part = reinterpret_cast<float*>(smem + L::kPartOff);  // [QW][128][TOK]
   named_bar_sync(1, kEpi);  // every consumer is done with the ring
-  // the k halves: beta 1 stores, beta 0 adds
-  auto frag = [&](int mt, int nt, int e) {  // (row, token) of accumulator element e
-    const int row = 32 * rp + 16 * mt + g + 8 * (e >> 1);
-    const int tok = nt * 8 + 2 * t + (e & 1);
-    return row * TOK + tok;
-  };
-  // in k order: group 2 beta, then 2 beta + 1, beta 0 before beta 1
-  if (beta == 1) {
+  // each warp's partial (its groups in k order), then the k parts summed in order
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) red[frag(mt, nt, e)] = acc[mt][0][nt][e] + acc[mt][1][nt][e];
-  }
-  named_bar_sync(1, kEpi);
-  if (beta == 0) {
+      for (int e = 0; e < 4; ++e) {
+        float a = acc[mt][0][nt][e];
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          red[frag(mt, nt, e)] = (acc[mt][0][nt][e] + acc[mt][1][nt][e]) + red[frag(mt, nt, e)];
-  }
+        for (int bb = 1; bb < GPW; ++bb) a += acc[mt][bb][nt][e];
+        const int row = 32 * rp + 16 * mt + g + 8 * (e >> 1);
+        const int tok = nt * 8 + 2 * t + (e & 1);
+        part[(qp * 128 + row) * TOK + tok] = a;
+      }
   pdl_wait();  // outputs, residuals and the workspace follow the preceding kernel
   const bool good = !named_bar_or(1, kEpi, !ok || *abort_flag);
-  // thread ct: row ct & 127, tokens (ct >> 7) + 2j
+  // thread ct: row ct & 127, tokens (ct >> 7) + QW j
   const int row = ct & 127, tpar = ct >> 7;
-  constexpr int TPT = TOK / 2;  // tokens a thread
+  constexpr int TPT = TOK / QW;  // tokens a thread
   float v[TPT];
 #pragma unroll
-  for (int j = 0; j < TPT; ++j) v[j] = red[row * TOK + tpar + 2 * j];
+  for (int j = 0; j < TPT; ++j) {
+    const int tok = tpar + QW * j;
+    float a = part[row * TOK + tok];
+#pragma unroll
+    for (int q = 1; q < QW; ++q) a += part[(q * 128 + row) * TOK + tok];
+    v[j] = a;
+  }
   bool last = true;
   if (KS > 1) {
     float* base = A.ws + static_cast<size_t>(bx) * KS * kQpRows * TOK + static_cast<size_t>(row) * TOK;
     if (good) {
       float* mine = base + static_cast<size_t>(ks) * kQpRows * TOK;
 #pragma unroll
-      for (int j = 0; j < TPT; ++j) mine[tpar + 2 * j] = v[j];
+      for (int j = 0; j < TPT; ++j) mine[tpar + QW * j] = v[j];
     }
     named_bar_sync(1, kEpi);
     if (ct == 0) {
@@ -361,14 +369,14 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
       for (int j = 0; j < TPT; ++j) v[j] = 0.f;
       for (int q = 0; q < KS; ++q) {
         const float* p = base + static_cast<size_t>(q) * kQpRows * TOK;
-        // the row's TOK floats; this thread's are tokens tpar, tpar + 2, ...
+        // the row's TOK floats; this thread's are tokens tpar, tpar + QW, ...
 #pragma unroll
         for (int c4 = 0; c4 < TOK / 4; ++c4) {
           const float4 f = ld_cg_f4(p + 4 * c4);
           const float fv[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            if ((4 * c4 + e) % 2 == tpar) v[(4 * c4 + e) / 2] += fv[e];
+            if ((4 * c4 + e) % QW == tpar) v[(4 * c4 + e) / QW] += fv[e];
         }
       }
     }
@@ -378,7 +386,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
     if (mode == EPI_SWIGLU || mode == EPI_ARGMAX) {
       named_bar_sync(2, kEpi);  // every thread has read red
 #pragma unroll
-      for (int j = 0; j < TPT; ++j) red[row * TOK + tpar + 2 * j] = v[j];
+      for (int j = 0; j < TPT; ++j) red[row * TOK + tpar + QW * j] = v[j];
       named_bar_sync(2, kEpi);
     }
     if (mode == EPI_SWIGLU) {
@@ -389,13 +397,13 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
       if (row < 64 && f < SG.rows) {
 #pragma unroll
         for (int j = 0; j < TPT; ++j) {
-          const int tok = tpar + 2 * j;
+          const int tok = tpar + QW * j;
           if (tok < M) out[tok * ldo + f] = f2bf(silu_f(round_bf(v[j])) * round_bf(red[(row + 64) * TOK + tok]));
         }
       }
     } else if (mode == EPI_ARGMAX) {
       // per token: the best (value, first index) key over the tile's rows;
-      // warp w holds rows 32 (w & 3) .. +31 of tokens (w >> 2) + 2j
+      // warp w holds rows 32 (w & 3) .. +31 of tokens (w >> 2) + QW j
       const int grow = tile * kQpRows + row;
 #pragma unroll
       for (int j = 0; j < TPT; ++j) {
@@ -406,7 +414,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
           const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
           k = other > k ? other : k;
         }
-        if (lane == 0) kbuf[(warp & 3) * TOK + tpar + 2 * j] = k;
+        if (lane == 0) kbuf[(warp & 3) * TOK + tpar + QW * j] = k;
       }
       named_bar_sync(2, kEpi);
       if (ct < TOK && ct < M) {
@@ -424,7 +432,7 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
       if (grow < SG.rows) {
 #pragma unroll
         for (int j = 0; j < TPT; ++j) {
-          const int tok = tpar + 2 * j;
+          const int tok = tpar + QW * j;
           if (tok >= M) continue;
           const size_t o = tok * ldo + grow;
           if (mode == EPI_F32) {
@@ -441,14 +449,14 @@ __global__ void __launch_bounds__(kGvThreads, 2) qmm_gemv_kernel(const __grid_co
 }
 
 int g_gv_sms = 0;
-bool g_gv_attr[2] = {false, false};
+bool g_gv_attr[2][2] = {{false, false}, {false, false}};
 
-template <int NT>
+template <int NT, int QW>
 int gv_set_attr() {
-  if (!g_gv_attr[NT - 1]) {
-    IAM_CUDA(cudaFuncSetAttribute(qmm_gemv_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  GvLayout<NT>::kSmem));
-    g_gv_attr[NT - 1] = true;
+  if (!g_gv_attr[NT - 1][QW / 4]) {
+    IAM_CUDA(cudaFuncSetAttribute(qmm_gemv_kernel<NT, QW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  GvLayout<NT, QW>::kSmem));
+    g_gv_attr[NT - 1][QW / 4] = true;
   }
   return IAM_OK;
 }
@@ -470,21 +478,21 @@ int gv_plan_ks(int tiles, int KB) {
   return std::max(ks, 1);
 }
 
-template <int NT>
+template <int NT, int QW>
 int gv_launch(const QmmGvArgs& ga, int ks, cudaStream_t st, bool pdl) {
-  const int r = gv_set_attr<NT>();
+  const int r = gv_set_attr<NT, QW>();
   if (r != IAM_OK) return r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ga.a.total_ctas, 1, ks);
-  cfg.blockDim = dim3(kGvThreads, 1, 1);
-  cfg.dynamicSmemBytes = GvLayout<NT>::kSmem;
+  cfg.blockDim = dim3(gv_threads(QW), 1, 1);
+  cfg.dynamicSmemBytes = GvLayout<NT, QW>::kSmem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  IAM_CUDA(cudaLaunchKernelEx(&cfg, qmm_gemv_kernel<NT>, ga));
+  IAM_CUDA(cudaLaunchKernelEx(&cfg, qmm_gemv_kernel<NT, QW>, ga));
   return IAM_OK;
 }
 
@@ -544,7 +552,12 @@ int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, siz
   const int r = tma_encode_2d(&ga.xmap, a.x, 2, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K), TOK, 64,
                               true, static_cast<uint64_t>(a.ldx));
   if (r != IAM_OK) return r;
-  return NT == 1 ? gv_launch<1>(ga, ks, st, pdl) : gv_launch<2>(ga, ks, st, pdl);
+  // 16 consumer warps (each converts one 64-k group of a block) by default;
+  // IAM_QMM_GEMV_WARPS=8 selects 8 (two groups each)
+  const char* wv = std::getenv("IAM_QMM_GEMV_WARPS");
+  const bool w8 = wv && std::atoi(wv) == 8;
+  if (NT == 1) return w8 ? gv_launch<1, 2>(ga, ks, st, pdl) : gv_launch<1, 4>(ga, ks, st, pdl);
+  return w8 ? gv_launch<2, 2>(ga, ks, st, pdl) : gv_launch<2, 4>(ga, ks, st, pdl);
 }
 
 }  // namespace iam

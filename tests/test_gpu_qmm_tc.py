@@ -106,15 +106,18 @@ def test_pack_layout_matches_restatement():
     assert np.array_equal(got, ref)
 
 
-@pytest.fixture(params=["default", "tensor_core", "gemv16"])
+@pytest.fixture(params=["default", "tensor_core", "gemv16", "gemv_8warps"])
 def kernel(request, monkeypatch):
     """The library's kernel choice (GEMV up to 8 tokens), the tensor-core
-    kernel at every width, or the GEMV kernel up to 16 tokens (its 16-token
-    tile)."""
+    kernel at every width, the GEMV kernel up to 16 tokens (its 16-token
+    tile), or the GEMV kernel with 8 consumer warps instead of 16."""
     if request.param == "tensor_core":
         monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "0")
     elif request.param == "gemv16":
         monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "16")
+    elif request.param == "gemv_8warps":
+        monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "16")
+        monkeypatch.setenv("IAM_QMM_GEMV_WARPS", "8")
     return request.param
 
 
