@@ -471,8 +471,10 @@ int gv_plan_ks(int tiles, int KB) {
     const int k = std::atoi(v);
     if (k >= 1) return std::min(k, KB);
   }
+  double per_sm = 1.8;  // target resident CTAs an SM (IAM_QMM_GEMV_CTAS overrides, for measurements)
+  if (const char* v = std::getenv("IAM_QMM_GEMV_CTAS")) per_sm = std::max(0.1, std::min(2.0, std::atof(v)));
   const int slots = 2 * g_gv_sms;
-  int ks = (static_cast<int>(1.8 * g_gv_sms) + tiles - 1) / tiles;
+  int ks = (static_cast<int>(per_sm * g_gv_sms) + tiles - 1) / tiles;
   if (static_cast<long>(tiles) * ks > slots) ks = slots / tiles;
   ks = std::min(ks, std::max(1, KB / 2));
   return std::max(ks, 1);
