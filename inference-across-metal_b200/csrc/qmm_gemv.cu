@@ -554,12 +554,13 @@ int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, siz
   const int r = tma_encode_2d(&ga.xmap, a.x, 2, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.K), TOK, 64,
                               true, static_cast<uint64_t>(a.ldx));
   if (r != IAM_OK) return r;
-  // 16 consumer warps (each converts one 64-k group of a block) by default;
-  // IAM_QMM_GEMV_WARPS=8 selects 8 (two groups each)
+  // 8 consumer warps (each converts two 64-k groups of a block) by default:
+  // measured faster than 16 (one group each), whose per-block overheads are
+  // spread over half the weights; IAM_QMM_GEMV_WARPS=16 selects 16
   const char* wv = std::getenv("IAM_QMM_GEMV_WARPS");
-  const bool w8 = wv && std::atoi(wv) == 8;
-  if (NT == 1) return w8 ? gv_launch<1, 2>(ga, ks, st, pdl) : gv_launch<1, 4>(ga, ks, st, pdl);
-  return w8 ? gv_launch<2, 2>(ga, ks, st, pdl) : gv_launch<2, 4>(ga, ks, st, pdl);
+  const bool w16 = wv && std::atoi(wv) == 16;
+  if (NT == 1) return w16 ? gv_launch<1, 4>(ga, ks, st, pdl) : gv_launch<1, 2>(ga, ks, st, pdl);
+  return w16 ? gv_launch<2, 4>(ga, ks, st, pdl) : gv_launch<2, 2>(ga, ks, st, pdl);
 }
 
 }  // namespace iam

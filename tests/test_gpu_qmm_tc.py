@@ -106,18 +106,18 @@ def test_pack_layout_matches_restatement():
     assert np.array_equal(got, ref)
 
 
-@pytest.fixture(params=["default", "tensor_core", "gemv16", "gemv_8warps"])
+@pytest.fixture(params=["default", "tensor_core", "gemv16", "gemv_16warps"])
 def kernel(request, monkeypatch):
     """The library's kernel choice (GEMV up to 8 tokens), the tensor-core
     kernel at every width, the GEMV kernel up to 16 tokens (its 16-token
-    tile), or the GEMV kernel with 8 consumer warps instead of 16."""
+    tile), or the GEMV kernel with 16 consumer warps instead of 8."""
     if request.param == "tensor_core":
         monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "0")
     elif request.param == "gemv16":
         monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "16")
-    elif request.param == "gemv_8warps":
+    elif request.param == "gemv_16warps":
         monkeypatch.setenv("IAM_QMM_GEMV_MAX_M", "16")
-        monkeypatch.setenv("IAM_QMM_GEMV_WARPS", "8")
+        monkeypatch.setenv("IAM_QMM_GEMV_WARPS", "16")
     return request.param
 
 
