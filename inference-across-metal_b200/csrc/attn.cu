@@ -427,13 +427,17 @@ __global__ void __launch_bounds__(128, 1) attn_decode_tc_kernel(const AttnArgs a
 }
 
 // ---------------------------------------------------------------- combine + gate
+// One CTA per (row, query head): warp w merges the splits w, w + 8, ... of
+// the head's partial outputs (each split's weight exp(m_i - max), from the
+// partial maxima every warp reads), the eight warps' sums meet in shared
+// memory and are added in warp order, then each thread finishes one of the
+// head's 256 dimensions with the attention output gate.
 __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
   pdl_wait();
   pdl_trigger();
-  const int t = blockIdx.x;
+  __shared__ float part[8][kHeadDim];
+  const int t = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y * 8 + warp;
-  if (h >= a.n_heads) return;
   const int ns = a.nsplit;  // <= 64
   const size_t base = (static_cast<size_t>(t) * a.n_heads + h) * ns;
   // lane i holds split i and i + 32: max, then each split's weight exp(m_i - max)
@@ -448,8 +452,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
             (lane + 32 < ns ? a.part_ml[2 * (base + lane + 32) + 1] * sc1 : 0.f);
   l = warp_sum(l);
   float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-  for (int c = 0; c < ns; ++c) {
+  for (int c = warp; c < ns; c += 8) {
     const float sc = __shfl_sync(0xffffffffu, c < 32 ? sc0 : sc1, c & 31);
     if (sc == 0.f) continue;
     const float4* po = reinterpret_cast<const float4*>(a.part_o + (base + c) * kHeadDim + 8 * lane);
@@ -457,19 +460,22 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     o[0] = fmaf(x0.x, sc, o[0]); o[1] = fmaf(x0.y, sc, o[1]); o[2] = fmaf(x0.z, sc, o[2]); o[3] = fmaf(x0.w, sc, o[3]);
     o[4] = fmaf(x1.x, sc, o[4]); o[5] = fmaf(x1.y, sc, o[5]); o[6] = fmaf(x1.z, sc, o[6]); o[7] = fmaf(x1.w, sc, o[7]);
   }
-  float r[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) part[warp][8 * lane + i] = o[i];
+  __syncthreads();
+  const int dim = threadIdx.x;  // 0 .. 255
+  float acc = part[0][dim];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) acc += part[w][dim];
+  float r;
   if (a.qkv) {  // attention output gate: the second half of each head's q_proj row
-    float gate[8];
-    unpack8(*reinterpret_cast<const uint4*>(a.qkv + static_cast<size_t>(t) * a.ld_qkv +
-                                            static_cast<size_t>(h) * 2 * kHeadDim + kHeadDim + 8 * lane),
-            gate);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) r[i] = round_bf(o[i] / l) * sigmoid_f(gate[i]);
+    const float gate = bf2f(a.qkv[static_cast<size_t>(t) * a.ld_qkv + static_cast<size_t>(h) * 2 * kHeadDim + kHeadDim +
+                                  dim]);
+    r = round_bf(acc / l) * sigmoid_f(gate);
   } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) r[i] = o[i] / l;
+    r = acc / l;
   }
-  *reinterpret_cast<uint4*>(a.out + static_cast<size_t>(t) * a.ld_out + h * kHeadDim + 8 * lane) = pack8(r);
+  a.out[static_cast<size_t>(t) * a.ld_out + h * kHeadDim + dim] = f2bf(r);
 }
 
 // copy_bf16 x2 (full_forward.swift:384-392, 909-924): append rows of k and v.
@@ -552,7 +558,8 @@ int launch_attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
 }
 
 int launch_attn_combine(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  return launch_k(attn_combine_kernel, dim3(a.rows, (a.n_heads + 7) / 8), dim3(256), 0, st, pdl, a);
+  IAM_CHECK(a.head_dim == kHeadDim, "attention combine: head_dim 256");
+  return launch_k(attn_combine_kernel, dim3(a.rows, a.n_heads), dim3(256), 0, st, pdl, a);
 }
 
 int attn_chunk_tokens() { return kChunkTok; }

@@ -3,19 +3,15 @@
 #include <cmath>
 
 #include "kernels.cuh"
+#include "rmsnorm.cuh"
 
 namespace iam {
 
 // ---------------------------------------------------------------- RMSNorm
 // rms_norm_bf16 (full_forward.swift:59-86), bit-exact with the reference's
-// summation order: the reference's thread i (of 256) sums x[i + 256 j] in j
-// order, then a shared-memory tree adds thread i + s into i for s = 128..1.
-// Here the CTA stages the row in shared memory with one round of 16-byte
-// loads; warp 0 plays all 256 threads: lane l owns virtual threads
-// 8l..8l+7; tree levels s >= 8 are lane shuffles (xor 16..1), s = 4, 2, 1 are
-// in-lane.  rms = sqrt(sum / dim + eps); then the whole CTA writes
-// out = bf16((x / rms) * w) with 16-byte accesses.
-// Requires dim % 256 == 0.
+// summation order (rmsnorm.cuh): the CTA stages the row in shared memory with
+// one round of 16-byte loads, warp 0 reduces it, then the whole CTA writes
+// out = bf16((x / rms) * w) with 16-byte accesses.  Requires dim % 256 == 0.
 __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restrict__ x, int ldx,
                                                        const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
                                                        int ldo, int dim, float eps) {
@@ -37,33 +33,8 @@ __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restric
   __syncthreads();
   __shared__ float rms_s;
   if (tid < 32) {
-    float p[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    const int nj = dim / 256;
-    for (int j = 0; j < nj; ++j) {
-      const uint4 v = xs[32 * j + tid];  // virtual threads 8 tid .. 8 tid + 7, element block j
-      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float a0 = lo_bf(u[i]), a1 = hi_bf(u[i]);
-        p[2 * i] += a0 * a0;
-        p[2 * i + 1] += a1 * a1;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float other = __shfl_xor_sync(0xffffffffu, p[i], o);
-        if (tid < o) p[i] += other;  // lanes >= o only feed lower lanes
-      }
-    if (tid == 0) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) p[i] += p[i + 4];
-      p[0] += p[2];
-      p[1] += p[3];
-      p[0] += p[1];
-      rms_s = sqrtf(p[0] / static_cast<float>(dim) + eps);
-    }
+    const float r = rms_row_warp([&](int i) { return xs[i]; }, dim, eps, tid);
+    if (tid == 0) rms_s = r;
   }
   __syncthreads();
   const float rms = rms_s;
@@ -72,14 +43,7 @@ __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restric
   for (int r = 0; r < 4; ++r) {
     const int i = tid + r * static_cast<int>(blockDim.x);
     if (i >= nv) break;
-    const uint4 v = xs[i];
-    const uint4 ww = wreg[r];
-    const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, wv[4] = {ww.x, ww.y, ww.z, ww.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      o[k] = pack_bf2((lo_bf(xv[k]) / rms) * lo_bf(wv[k]), (hi_bf(xv[k]) / rms) * hi_bf(wv[k]));
-    *reinterpret_cast<uint4*>(orow + 8 * i) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(orow + 8 * i) = rms_apply8(xs[i], wreg[r], rms);
   }
 }
 

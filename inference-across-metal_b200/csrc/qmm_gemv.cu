@@ -39,6 +39,7 @@
 #include <type_traits>
 
 #include "kernels.cuh"
+#include "rmsnorm.cuh"
 #include "tc.cuh"
 #include "tma.cuh"
 
@@ -445,6 +446,24 @@ __global__ void __launch_bounds__(gv_threads(QW), 2) qmm_gemv_kernel(const __gri
         }
       }
     }
+  }
+  if (A.norm_out && last) {
+    // The fused RMSNorm of the residual rows just written: the CTA that saw
+    // the pass's last tile arrive normalises every row (one warp a row).  The
+    // barrier orders this CTA's stores before one GPU-scope acquire-release
+    // arrival (cumulative: it publishes them and, for the last arrival,
+    // acquires every other tile's).
+    named_bar_sync(1, kEpi);
+    if (ct == 0) {
+      int prev;
+      asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(A.norm_done) : "memory");
+      const int l = prev == A.total_ctas - 1;
+      if (l) *A.norm_done = 0;
+      *last_flag = l;
+    }
+    named_bar_sync(1, kEpi);
+    if (*last_flag && good)
+      rms_norm_rows_warp(SG.out, SG.ldo, A.norm_w, A.norm_out, A.ldn, M, SG.rows, A.norm_eps, warp, kGvWarps, lane);
   }
 }
 
