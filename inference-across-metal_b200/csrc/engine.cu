@@ -806,7 +806,10 @@ int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, c
     a.seg[0].ldo = H;
     a.seg[0].resid = resid;
     a.seg[0].ldr = H;
-    if (norm_w) {
+    // the fused RMSNorm only on narrow steps (the GEMV path; a single CTA
+    // normalises every row, which costs more than the norm kernel at wide K)
+    const char* fn = std::getenv("IAM_FUSED_NORM");  // "0": the norm kernel always (measurements)
+    if (norm_w && M <= std::min(qmm_gemv_max_m(), 8) && !(fn && fn[0] == '0')) {
       a.norm_w = norm_w;
       a.norm_out = e.normed;
       a.ldn = H;

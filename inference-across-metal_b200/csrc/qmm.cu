@@ -898,9 +898,11 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
       }
       if (p.norm_out) p.norm_out += static_cast<size_t>(m0) * p.ldn;
       // narrow passes convert the weights in registers (mma.sync); wider ones
-      // on the tensor cores
-      const int r = p.M <= qmm_gemv_max_m() ? qmm_gemv_run(p, st, pdl, ws_floats_cap, ws_ctr_cap)
-                                            : qmm_tc_run(p, st, pdl, ws_floats_cap, ws_ctr_cap);
+      // on the tensor cores (which have no fused RMSNorm)
+      const bool gemv = p.M <= qmm_gemv_max_m();
+      IAM_CHECK(gemv || !p.norm_out, "qmm: the fused RMSNorm runs on the GEMV path only (narrow passes)");
+      const int r = gemv ? qmm_gemv_run(p, st, pdl, ws_floats_cap, ws_ctr_cap)
+                         : qmm_tc_run(p, st, pdl, ws_floats_cap, ws_ctr_cap);
       if (r != IAM_OK) return r;
     }
     return IAM_OK;

@@ -462,8 +462,9 @@ __global__ void __launch_bounds__(gv_threads(QW), 2) qmm_gemv_kernel(const __gri
       *last_flag = l;
     }
     named_bar_sync(1, kEpi);
-    if (*last_flag && good)
-      rms_norm_rows_warp(SG.out, SG.ldo, A.norm_w, A.norm_out, A.ldn, M, SG.rows, A.norm_eps, warp, kGvWarps, lane);
+    if (*last_flag && good)  // the idle ring holds the rows (M <= 16 rows of dim <= 5120: checked on the host)
+      rms_norm_rows_cta(SG.out, SG.ldo, A.norm_w, A.norm_out, A.ldn, M, SG.rows, A.norm_eps,
+                        reinterpret_cast<uint4*>(smem), reinterpret_cast<float*>(smem + L::kBarOff - 64), ct, kEpi, 1);
   }
 }
 
@@ -549,6 +550,10 @@ int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, siz
   }
   a.total_ctas = cta;
   const int NT = a.M <= 8 ? 1 : 2;
+  if (a.norm_out)  // the fused RMSNorm stages the pass's rows in the idle ring
+    IAM_CHECK(static_cast<size_t>(a.M) * a.seg[0].rows * 2 + 64 <=
+                  static_cast<size_t>(NT == 1 ? GvLayout<1, 2>::kBarOff : GvLayout<2, 2>::kBarOff),
+              "qmm: the fused RMSNorm's rows do not fit in shared memory");
   const int TOK = 8 * NT;
   const int KB = qp_kblocks(a.K);
   int ks = gv_plan_ks(cta, KB);

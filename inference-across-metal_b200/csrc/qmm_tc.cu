@@ -39,7 +39,6 @@
 #include <cstring>
 
 #include "kernels.cuh"
-#include "rmsnorm.cuh"
 #include "tc.cuh"
 #include "tma.cuh"
 
@@ -510,25 +509,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
           }
         }
       }
-    }
-    if (A.norm_out && last) {
-      // The fused RMSNorm of the residual rows just written: the CTA that saw
-      // the pass's last tile arrive normalises every row (one warp a row).
-      // The barrier orders this CTA's stores before one GPU-scope
-      // acquire-release arrival (cumulative: it publishes them and, for the
-      // last arrival, acquires every other tile's).
-      named_bar_sync(1, 32 * kTcDqWarps);
-      if (threadIdx.x == 64) {
-        int prev;
-        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(A.norm_done) : "memory");
-        const int l = prev == A.total_ctas - 1;
-        if (l) *A.norm_done = 0;
-        *last_flag = l;
-      }
-      named_bar_sync(1, 32 * kTcDqWarps);
-      if (*last_flag && ok)
-        rms_norm_rows_warp(S.out, S.ldo, A.norm_w, A.norm_out, A.ldn, A.M, S.rows, A.norm_eps, warp - 2, kTcDqWarps,
-                           lane);
     }
   }
 

@@ -63,21 +63,42 @@ __device__ __forceinline__ uint4 ld_cg_u4(const void* p) {
   return r;
 }
 
-// The rows of the residual stream written by every CTA of a matmul, each
-// normalised by one warp: row m of x (ldx) -> row m of out (ldo).  Called by
-// the one CTA that saw the matmul's last tile arrive; `warps` warps of it take
-// rows in turn (warp index `warp`).  The rows are read from L2: other CTAs
-// wrote them, published by the acquire-release arrival count.
-__device__ __forceinline__ void rms_norm_rows_warp(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out,
-                                                   int ldo, int rows, int dim, float eps, int warp, int warps,
-                                                   int lane) {
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// The rows of the residual stream written by every CTA of a matmul,
+// normalised by the one CTA that saw the matmul's last tile arrive: rows
+// m < rows of x (ldx, dim bf16 each; rows * dim * 2 bytes must fit in `stage`)
+// -> out (ldo).  The CTA's `threads` threads (ids tid, bar_id a named barrier
+// over exactly them) copy the rows into shared memory with asynchronous
+// 16-byte copies (all in flight at once, read from L2: other CTAs wrote them,
+// published by the acquire-release arrival count), each warp reduces its
+// rows, then every thread writes normalised chunks.
+__device__ __forceinline__ void rms_norm_rows_cta(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out,
+                                                  int ldo, int rows, int dim, float eps, uint4* stage, float* rms_s,
+                                                  int tid, int threads, int bar_id) {
+  const int nv = dim / 8;
+  for (int i = tid; i < rows * nv; i += threads) {
+    const int m = i / nv, c = i - m * nv;
+    cp_async16(stage + i, x + static_cast<size_t>(m) * ldx + 8 * c);
+  }
+  cp_async_wait_all();
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(threads) : "memory");
+  const int warp = tid >> 5, lane = tid & 31, warps = threads >> 5;
   for (int m = warp; m < rows; m += warps) {
-    const uint16_t* xr = x + static_cast<size_t>(m) * ldx;
-    const float rms = rms_row_warp([&](int i) { return ld_cg_u4(xr + 8 * i); }, dim, eps, lane);
-    uint16_t* orow = out + static_cast<size_t>(m) * ldo;
-    for (int i = lane; i < dim / 8; i += 32)
-      *reinterpret_cast<uint4*>(orow + 8 * i) =
-          rms_apply8(ld_cg_u4(xr + 8 * i), *reinterpret_cast<const uint4*>(w + 8 * i), rms);
+    const uint4* xr = stage + m * nv;
+    const float r = rms_row_warp([&](int i) { return xr[i]; }, dim, eps, lane);
+    if (lane == 0) rms_s[m] = r;
+  }
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(threads) : "memory");
+  for (int c = tid; c < nv; c += threads) {
+    const uint4 ww = *reinterpret_cast<const uint4*>(w + 8 * c);
+    for (int m = 0; m < rows; ++m)
+      *reinterpret_cast<uint4*>(out + static_cast<size_t>(m) * ldo + 8 * c) = rms_apply8(stage[m * nv + c], ww, rms_s[m]);
   }
 }
 
