@@ -159,7 +159,6 @@ struct EngineImpl {
   uint16_t* gin = nullptr;  // [n_gdn][max_rows][ld_in]: each GDN layer's projections of the last block
   float *part_o = nullptr, *part_ml = nullptr, *red32 = nullptr;
   float* qws = nullptr;  // split-K workspace of the matmuls (zero between launches)
-  int* norm_done = nullptr;  // tile arrivals of the matmul whose last CTA writes the fused RMSNorm (zero between launches)
   int* qctr = nullptr;
   size_t qws_floats = 0, qctr_n = 0;
   unsigned long long* keys = nullptr;
@@ -476,8 +475,6 @@ int alloc_all(EngineImpl& e) {
   E_CUDA(cudaMalloc(&e.d_out, sizeof(int32_t) * (1 + R)));
   E_CUDA(cudaMalloc(&e.d_err, sizeof(int)));
   E_CUDA(cudaMemset(e.d_err, 0, sizeof(int)));
-  E_CUDA(cudaMalloc(&e.norm_done, sizeof(int)));
-  E_CUDA(cudaMemset(e.norm_done, 0, sizeof(int)));
   E_CUDA(cudaMallocHost(&e.h_in, sizeof(int32_t) * (1 + R)));
   E_CUDA(cudaMallocHost(&e.h_out, sizeof(int32_t) * (1 + R)));
   E_CUDA(cudaMallocHost(&e.h_err, sizeof(int)));
@@ -575,12 +572,8 @@ int run_qmm(EngineImpl& e, QmmArgs& a, const char* kind, double bytes) {
 }
 
 // Row-parallel matmul (K sharded) followed by the residual add: fused on one
-// GPU; fp32 partials + NCCL all-reduce + residual kernel across GPUs.  With
-// norm_w on one GPU the matmul's last CTA also writes rms_norm(out, norm_w)
-// into e.normed (the next block's input) and the function returns true in
-// *normed; otherwise the caller runs the RMSNorm kernel.
-int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, const uint16_t* resid, uint16_t* out,
-                       const uint16_t* norm_w, bool* normed);
+// GPU; fp32 partials + NCCL all-reduce + residual kernel across GPUs.
+int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, const uint16_t* resid, uint16_t* out);
 
 // The GDN kernel's arguments for layer L over the first `rows` rows of each
 // of n_seq sequences (slots 0..n_seq-1; sequence q's rows follow the q * rows
@@ -619,14 +612,11 @@ GdnArgs gdn_args(EngineImpl& e, const Layer& L, int rows, int n_seq) {
   return g;
 }
 
-// normed_in: e.normed already holds rms_norm(e.hidden, L.in_norm) (written by
-// the previous layer's down_proj); *normed_out: e.normed holds the MLP's input
-// norm when this returns.
-int enqueue_gdn(EngineImpl& e, const Layer& L, int K, bool normed_in, bool* normed_out) {
+int enqueue_gdn(EngineImpl& e, const Layer& L, int K) {
   const iam_dims& d = e.d;
   const int H = d.hidden;
   uint16_t* const in = e.gin + static_cast<size_t>(L.idx) * d.max_rows * e.ld_in;
-  if (!normed_in) {
+  {
     Recorder rec(e, "rmsnorm", 4.0 * K * H);
     E_RUN(launch_rms_norm(e.hidden, H, L.in_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
   }
@@ -652,14 +642,14 @@ int enqueue_gdn(EngineImpl& e, const Layer& L, int K, bool normed_in, bool* norm
     Recorder rec(e, "gdn", 2.0 * e.gv_l * d.gdn_dk * d.gdn_dv * 4 + 2.0 * 3 * e.conv_l * 2);
     E_RUN(launch_gdn(g, e.stream, e.pdl));
   }
-  E_RUN(row_parallel_resid(e, L.out, e.mid, e.vd_l, e.hidden, e.resid, L.post_norm, normed_out));
+  E_RUN(row_parallel_resid(e, L.out, e.mid, e.vd_l, e.hidden, e.resid));
   return IAM_OK;
 }
 
-int enqueue_attn(EngineImpl& e, const Layer& L, int K, bool normed_in, bool* normed_out) {
+int enqueue_attn(EngineImpl& e, const Layer& L, int K) {
   const iam_dims& d = e.d;
   const int H = d.hidden, hd = d.head_dim;
-  if (!normed_in) {
+  {
     Recorder rec(e, "rmsnorm", 4.0 * K * H);
     E_RUN(launch_rms_norm(e.hidden, H, L.in_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
   }
@@ -723,16 +713,14 @@ int enqueue_attn(EngineImpl& e, const Layer& L, int K, bool normed_in, bool* nor
     Recorder rec(e, "attn_combine", 4.0 * K * e.hq_l * kNSplit * hd);
     E_RUN(launch_attn_combine(t, e.stream, e.pdl));
   }
-  E_RUN(row_parallel_resid(e, L.o, e.mid, e.hq_l * hd, e.hidden, e.resid, L.post_norm, normed_out));
+  E_RUN(row_parallel_resid(e, L.o, e.mid, e.hq_l * hd, e.hidden, e.resid));
   return IAM_OK;
 }
 
-// next_norm: the norm weights of what follows the MLP (the next layer's input
-// norm, or the final norm); *normed_out: e.normed holds that norm of e.hidden.
-int enqueue_mlp(EngineImpl& e, const Layer& L, int K, bool normed_in, const uint16_t* next_norm, bool* normed_out) {
+int enqueue_mlp(EngineImpl& e, const Layer& L, int K) {
   const iam_dims& d = e.d;
   const int H = d.hidden;
-  if (!normed_in) {
+  {
     Recorder rec(e, "rmsnorm", 4.0 * K * H);
     E_RUN(launch_rms_norm(e.resid, H, L.post_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
   }
@@ -750,7 +738,7 @@ int enqueue_mlp(EngineImpl& e, const Layer& L, int K, bool normed_in, const uint
   a.seg[0].out = e.mlp_h;
   a.seg[0].ldo = e.inter_l;
   E_RUN(run_qmm(e, a, "qmm", qbytes(L.gate) + qbytes(L.up)));
-  E_RUN(row_parallel_resid(e, L.down, e.mlp_h, e.inter_l, e.resid, e.hidden, next_norm, normed_out));
+  E_RUN(row_parallel_resid(e, L.down, e.mlp_h, e.inter_l, e.resid, e.hidden));
   return IAM_OK;
 }
 
@@ -790,10 +778,8 @@ int enqueue_rollback(EngineImpl& e, int K, int n_keep, cudaStream_t st) {
 }
 
 
-int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, const uint16_t* resid, uint16_t* out,
-                       const uint16_t* norm_w, bool* normed) {
+int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, const uint16_t* resid, uint16_t* out) {
   const int H = e.d.hidden, M = e.cur_rows;
-  *normed = false;
   QmmArgs a = {};
   a.x = x;
   a.ldx = ldx;
@@ -806,17 +792,6 @@ int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, c
     a.seg[0].ldo = H;
     a.seg[0].resid = resid;
     a.seg[0].ldr = H;
-    // the fused RMSNorm only on narrow steps (the GEMV path; a single CTA
-    // normalises every row, which costs more than the norm kernel at wide K)
-    const char* fn = std::getenv("IAM_FUSED_NORM");  // "0": the norm kernel always (measurements)
-    if (norm_w && M <= std::min(qmm_gemv_max_m(), 8) && !(fn && fn[0] == '0')) {
-      a.norm_w = norm_w;
-      a.norm_out = e.normed;
-      a.ldn = H;
-      a.norm_eps = e.d.eps;
-      a.norm_done = e.norm_done;
-      *normed = true;
-    }
     return run_qmm(e, a, "qmm", qbytes(q));
   }
   seg_of(a.seg[0], q, EPI_F32);
@@ -884,19 +859,12 @@ int enqueue_step(EngineImpl& e, int n_seq, int Kseq) {
     Recorder rec(e, "embed", 4.0 * K * d.hidden);
     E_RUN(launch_embed_bf16(e.embed, tokens, e.hidden, K, d.hidden, d.vocab, e.d_err, e.stream, false));
   }
-  // On one GPU each residual matmul also writes the next RMSNorm (its last
-  // CTA, see QmmArgs::norm_out): only the first layer's input norm runs as a
-  // kernel of its own.
-  bool normed = false;
-  for (size_t i = 0; i < e.layers.size(); ++i) {
-    const Layer& L = e.layers[i];
-    bool mid_normed = false;
-    if (L.attn) E_RUN(enqueue_attn(e, L, K, normed, &mid_normed));
-    else E_RUN(enqueue_gdn(e, L, K, normed, &mid_normed));
-    const uint16_t* next = i + 1 < e.layers.size() ? e.layers[i + 1].in_norm : e.final_norm;
-    E_RUN(enqueue_mlp(e, L, K, mid_normed, next, &normed));
+  for (const Layer& L : e.layers) {
+    if (L.attn) E_RUN(enqueue_attn(e, L, K));
+    else E_RUN(enqueue_gdn(e, L, K));
+    E_RUN(enqueue_mlp(e, L, K));
   }
-  if (!normed) {
+  {
     Recorder rec(e, "rmsnorm", 4.0 * K * d.hidden);
     E_RUN(launch_rms_norm(e.hidden, d.hidden, e.final_norm, e.normed, d.hidden, K, d.hidden, d.eps, e.stream, e.pdl));
   }
@@ -1145,7 +1113,7 @@ extern "C" void iam_destroy(iam_engine* eng) {
   if (e.comm) iam::nccl_destroy(e.comm);
   void* bufs[] = {e.pool, e.ppool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
                   e.mid, e.mlp_h, e.q_buf, e.part_o, e.part_ml, e.red32, e.keys, e.best, e.rope_cs, e.d_in, e.d_out,
-                  e.d_err, e.qws, e.qctr, e.gin, e.d_bin, e.d_bout, e.norm_done};
+                  e.d_err, e.qws, e.qctr, e.gin, e.d_bin, e.d_bout};
   for (void* p : bufs)
     if (p) cudaFree(p);
   for (void* p : {static_cast<void*>(e.h_in), static_cast<void*>(e.h_out), static_cast<void*>(e.h_bin),

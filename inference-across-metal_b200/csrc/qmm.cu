@@ -875,11 +875,6 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
   IAM_CHECK(a.nseg >= 1 && a.nseg <= kQmmMaxSeg, "qmm: 1..4 segments");
   IAM_CHECK(aligned16(a.x) && a.ldx % 8 == 0, "qmm: x must be 16-byte aligned with ldx % 8 == 0");
   bool packed = a.seg[0].packed != nullptr;
-  if (a.norm_out)
-    IAM_CHECK(packed && a.nseg == 1 && a.seg[0].mode == EPI_RESID && a.norm_w && a.norm_done && a.ldn >= a.seg[0].rows &&
-                  a.seg[0].rows % 256 == 0 && a.seg[0].ldo % 8 == 0 && a.ldn % 8 == 0 && aligned16(a.seg[0].out) &&
-                  aligned16(a.norm_out) && aligned16(a.norm_w),
-              "qmm: the fused RMSNorm needs one packed EPI_RESID segment with 16-byte aligned rows of a multiple of 256");
   for (int i = 1; i < a.nseg; ++i)
     IAM_CHECK((a.seg[i].packed != nullptr) == packed, "qmm: segments mix packed and MLX-layout weights");
   if (packed) {
@@ -896,13 +891,10 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
         if (s.resid) s.resid += static_cast<size_t>(m0) * s.ldr;
         if (s.keys) s.keys += m0;
       }
-      if (p.norm_out) p.norm_out += static_cast<size_t>(m0) * p.ldn;
       // narrow passes convert the weights in registers (mma.sync); wider ones
-      // on the tensor cores (which have no fused RMSNorm)
-      const bool gemv = p.M <= qmm_gemv_max_m();
-      IAM_CHECK(gemv || !p.norm_out, "qmm: the fused RMSNorm runs on the GEMV path only (narrow passes)");
-      const int r = gemv ? qmm_gemv_run(p, st, pdl, ws_floats_cap, ws_ctr_cap)
-                         : qmm_tc_run(p, st, pdl, ws_floats_cap, ws_ctr_cap);
+      // on the tensor cores
+      const int r = p.M <= qmm_gemv_max_m() ? qmm_gemv_run(p, st, pdl, ws_floats_cap, ws_ctr_cap)
+                                            : qmm_tc_run(p, st, pdl, ws_floats_cap, ws_ctr_cap);
       if (r != IAM_OK) return r;
     }
     return IAM_OK;

@@ -56,16 +56,6 @@ struct QmmArgs {
   // consumers' first wait is on a phase that nothing completes and must run
   // out (nothing is in flight when the CTA exits).
   int starve;
-  // Optional with one EPI_RESID segment on the GEMV path: once every tile of
-  // the pass has stored its rows of out, the CTA that saw the last tile
-  // arrive (counted in *norm_done, which it re-zeroes) writes norm_out[m] =
-  // rms_norm_bf16(out[m], norm_w) for the pass's rows (rmsnorm.cuh: the
-  // reference's summation order).
-  const uint16_t* norm_w;
-  uint16_t* norm_out;
-  int ldn;
-  float norm_eps;
-  int* norm_done;
   QmmSeg seg[kQmmMaxSeg];
 };
 

@@ -39,7 +39,6 @@
 #include <type_traits>
 
 #include "kernels.cuh"
-#include "rmsnorm.cuh"
 #include "tc.cuh"
 #include "tma.cuh"
 
@@ -447,25 +446,6 @@ __global__ void __launch_bounds__(gv_threads(QW), 2) qmm_gemv_kernel(const __gri
       }
     }
   }
-  if (A.norm_out && last) {
-    // The fused RMSNorm of the residual rows just written: the CTA that saw
-    // the pass's last tile arrive normalises every row (one warp a row).  The
-    // barrier orders this CTA's stores before one GPU-scope acquire-release
-    // arrival (cumulative: it publishes them and, for the last arrival,
-    // acquires every other tile's).
-    named_bar_sync(1, kEpi);
-    if (ct == 0) {
-      int prev;
-      asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(A.norm_done) : "memory");
-      const int l = prev == A.total_ctas - 1;
-      if (l) *A.norm_done = 0;
-      *last_flag = l;
-    }
-    named_bar_sync(1, kEpi);
-    if (*last_flag && good)  // the idle ring holds the rows (M <= 16 rows of dim <= 5120: checked on the host)
-      rms_norm_rows_cta(SG.out, SG.ldo, A.norm_w, A.norm_out, A.ldn, M, SG.rows, A.norm_eps,
-                        reinterpret_cast<uint4*>(smem), reinterpret_cast<float*>(smem + L::kBarOff - 64), ct, kEpi, 1);
-  }
 }
 
 int g_gv_sms = 0;
@@ -550,10 +530,6 @@ int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, siz
   }
   a.total_ctas = cta;
   const int NT = a.M <= 8 ? 1 : 2;
-  if (a.norm_out)  // the fused RMSNorm stages the pass's rows in the idle ring
-    IAM_CHECK(static_cast<size_t>(a.M) * a.seg[0].rows * 2 + 64 <=
-                  static_cast<size_t>(NT == 1 ? GvLayout<1, 2>::kBarOff : GvLayout<2, 2>::kBarOff),
-              "qmm: the fused RMSNorm's rows do not fit in shared memory");
   const int TOK = 8 * NT;
   const int KB = qp_kblocks(a.K);
   int ks = gv_plan_ks(cta, KB);

@@ -3,9 +3,7 @@
 // x[i + 256 j]^2 in j order, then a shared-memory tree adds thread i + s into
 // i for s = 128..1.  One warp plays all 256 threads: lane l owns virtual
 // threads 8l..8l+7; tree levels s >= 8 are lane shuffles (xor 16..1),
-// s = 4, 2, 1 are in-lane.  Shared by the RMSNorm kernel and the matmul
-// epilogue that normalises the residual stream it just wrote, so both give
-// the same bits.
+// s = 4, 2, 1 are in-lane.
 #pragma once
 #include "common.cuh"
 
@@ -55,51 +53,6 @@ __device__ __forceinline__ uint4 rms_apply8(uint4 v, uint4 ww, float rms) {
   for (int k = 0; k < 4; ++k)
     o[k] = pack_bf2((lo_bf(xv[k]) / rms) * lo_bf(wv[k]), (hi_bf(xv[k]) / rms) * hi_bf(wv[k]));
   return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-__device__ __forceinline__ uint4 ld_cg_u4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-  return r;
-}
-
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
-               "l"(gmem_src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-// The rows of the residual stream written by every CTA of a matmul,
-// normalised by the one CTA that saw the matmul's last tile arrive: rows
-// m < rows of x (ldx, dim bf16 each; rows * dim * 2 bytes must fit in `stage`)
-// -> out (ldo).  The CTA's `threads` threads (ids tid, bar_id a named barrier
-// over exactly them) copy the rows into shared memory with asynchronous
-// 16-byte copies (all in flight at once, read from L2: other CTAs wrote them,
-// published by the acquire-release arrival count), each warp reduces its
-// rows, then every thread writes normalised chunks.
-__device__ __forceinline__ void rms_norm_rows_cta(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out,
-                                                  int ldo, int rows, int dim, float eps, uint4* stage, float* rms_s,
-                                                  int tid, int threads, int bar_id) {
-  const int nv = dim / 8;
-  for (int i = tid; i < rows * nv; i += threads) {
-    const int m = i / nv, c = i - m * nv;
-    cp_async16(stage + i, x + static_cast<size_t>(m) * ldx + 8 * c);
-  }
-  cp_async_wait_all();
-  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(threads) : "memory");
-  const int warp = tid >> 5, lane = tid & 31, warps = threads >> 5;
-  for (int m = warp; m < rows; m += warps) {
-    const uint4* xr = stage + m * nv;
-    const float r = rms_row_warp([&](int i) { return xr[i]; }, dim, eps, lane);
-    if (lane == 0) rms_s[m] = r;
-  }
-  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(threads) : "memory");
-  for (int c = tid; c < nv; c += threads) {
-    const uint4 ww = *reinterpret_cast<const uint4*>(w + 8 * c);
-    for (int m = 0; m < rows; ++m)
-      *reinterpret_cast<uint4*>(out + static_cast<size_t>(m) * ldo + 8 * c) = rms_apply8(stage[m * nv + c], ww, rms_s[m]);
-  }
 }
 
 }  // namespace iam
