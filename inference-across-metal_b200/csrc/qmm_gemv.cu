@@ -45,7 +45,11 @@
 namespace iam {
 namespace {
 
-constexpr int kGvStages = 4;
+constexpr int kGvStages = 3;
+// Resident CTAs an SM: with 8-token passes three fit, so while a launch runs
+// two an SM the next kernel's CTAs can start early (programmatic dependent
+// launch) and prefetch their weights; 16-token passes fit two.
+__host__ __device__ constexpr int gv_min_ctas(int NT) { return NT == 1 ? 3 : 2; }
 // QW: the number of consumer warps sharing one 32-row pair of a block, each
 // taking 4 / QW of its four 64-k groups; 4 QW consumer warps + 1 producer.
 __host__ __device__ constexpr int gv_warps(int QW) { return 4 * QW; }
@@ -69,7 +73,7 @@ struct GvLayout {
   static constexpr int kRedBytes = 128 * kTok * 4;
   static constexpr int kPartOff = kRedBytes + 4 * kTok * 8;
   static_assert(kPartOff + QW * kRedBytes <= kBarOff, "epilogue buffers fit in the ring");
-  static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
+  static_assert(gv_min_ctas(NT) * (kSmem + 1024) <= 228 * 1024, "resident CTAs per SM");
   static_assert(sizeof(QmmSeg) <= 128, "segment copy");
 };
 
@@ -111,7 +115,7 @@ struct QmmGvArgs {
 };
 
 template <int NT, int QW>
-__global__ void __launch_bounds__(gv_threads(QW), 2) qmm_gemv_kernel(const __grid_constant__ QmmGvArgs T) {
+__global__ void __launch_bounds__(gv_threads(QW), gv_min_ctas(NT)) qmm_gemv_kernel(const __grid_constant__ QmmGvArgs T) {
   using L = GvLayout<NT, QW>;
   constexpr int S = kGvStages, TOK = L::kTok;
   constexpr int kGvWarps = gv_warps(QW);
