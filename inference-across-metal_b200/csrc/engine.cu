@@ -163,6 +163,17 @@ struct EngineImpl {
   size_t qws_floats = 0, qctr_n = 0;
   unsigned long long* keys = nullptr;
   unsigned long long* best = nullptr;      // [world][max_rows] (TP)
+  // Row-parallel sums over peer memory (world > 1): this rank's receive area,
+  // [2 alternating buffers][world slots][max_rows][hidden] fp32 partials and
+  // then [2][hidden / 128] arrival counters; every rank's area mapped here
+  // through CUDA IPC (tp_peer[rank] is this rank's own).  Off (tp_p2p false):
+  // NCCL all-reduce of the partials and a residual kernel.
+  char* tp_area = nullptr;
+  char* tp_peer[kQmmMaxPeers] = {};
+  size_t tp_ctr_off = 0;
+  int tp_tiles = 0;
+  bool tp_p2p = false;
+  int rp_idx = 0;  // row-parallel matmuls enqueued so far in the current step
   int lm_ctas = 0;
   float* rope_cs = nullptr;
   StepIn* d_in = nullptr;
@@ -749,6 +760,48 @@ __global__ void resid_from_f32_kernel(const float* y, const uint16_t* resid, uin
     out[i] = f2bf(bf2f(resid[i]) + round_bf(y[i]));
 }
 
+// The row-parallel sum across GPUs plus the residual, one CTA per 128-column
+// tile: waits (bounded, on the GPU's global timer) until every rank's every
+// pass of the tile has arrived in this rank's receive slots, re-arms the
+// counter, then out = bf16(resid + bf16(sum of the ranks' partials in rank
+// order)) -- every rank computes the same bits.
+__global__ void __launch_bounds__(512) tp_reduce_resid_kernel(const float* __restrict__ recv, int* ctr, int world,
+                                                              size_t slot, int expect, int M, int H,
+                                                              const uint16_t* __restrict__ resid,
+                                                              uint16_t* __restrict__ out, int* err,
+                                                              unsigned long long limit_ns) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int ok;
+  const int tile = blockIdx.x;
+  if (threadIdx.x == 0) {
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    int v;
+    for (;;) {
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr + tile) : "memory");
+      if (v >= expect) break;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > limit_ns) break;
+      __nanosleep(128);
+    }
+    ok = v >= expect;
+    if (ok) ctr[tile] = 0;
+    else atomicCAS(err, 0, IAM_ETIMEOUT);
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int c0 = tile * 128;
+  for (int i = threadIdx.x; i < M * 128; i += blockDim.x) {
+    const int c = c0 + (i & 127);
+    if (c >= H) continue;
+    const size_t o = static_cast<size_t>(i >> 7) * H + c;
+    float sum = __ldcg(recv + o);
+    for (int r = 1; r < world; ++r) sum += __ldcg(recv + r * slot + o);
+    out[o] = f2bf(bf2f(resid[o]) + round_bf(sum));
+  }
+}
+
 __global__ void advance_kernel(StepIn* in, int* parity, int K) {
   in->pos += K;
   *parity ^= 1;
@@ -795,8 +848,31 @@ int row_parallel_resid(EngineImpl& e, const QW& q, const uint16_t* x, int ldx, c
     return run_qmm(e, a, "qmm", qbytes(q));
   }
   seg_of(a.seg[0], q, EPI_F32);
-  a.seg[0].out32 = e.red32;
   a.seg[0].ldo = H;
+  if (e.tp_p2p) {
+    // alternating buffers: a rank writes buffer b again only after its own sum
+    // over the other buffer, which waited for every peer's partial of that
+    // matmul -- pushed after the peer's sum over buffer b had finished
+    const int b = e.rp_idx++ & 1;
+    const size_t slot = static_cast<size_t>(e.d.max_rows) * H;
+    auto data = [&](char* area) {
+      return reinterpret_cast<float*>(area) + static_cast<size_t>(b) * e.world * slot;
+    };
+    auto ctr = [&](char* area) { return reinterpret_cast<int*>(area + e.tp_ctr_off) + b * e.tp_tiles; };
+    a.npush = e.world;
+    for (int i = 0; i < e.world; ++i) {  // this rank's own slot first, then the peers in ring order
+      const int r = (e.rank + i) % e.world;
+      a.push[i] = data(e.tp_peer[r]) + static_cast<size_t>(e.rank) * slot;
+      a.push_ctr[i] = ctr(e.tp_peer[r]);
+    }
+    E_RUN(run_qmm(e, a, "qmm", qbytes(q)));
+    Recorder rec(e, "tp_reduce", 4.0 * M * H * e.world + 4.0 * M * H);
+    const unsigned long long limit_ns = 1000000ull * static_cast<unsigned long long>(e.d.comm_timeout_ms > 0 ? e.d.comm_timeout_ms : 120000);
+    return launch_k(tp_reduce_resid_kernel, dim3(e.tp_tiles), dim3(512), 0, e.stream, e.pdl,
+                    static_cast<const float*>(data(e.tp_area)), ctr(e.tp_area), e.world, slot,
+                    e.world * qmm_packed_passes(M), M, H, resid, out, e.d_err, limit_ns);
+  }
+  a.seg[0].out32 = e.red32;
   E_RUN(run_qmm(e, a, "qmm", qbytes(q)));
   {
     Recorder rec(e, "allreduce", 4.0 * M * H);
@@ -854,6 +930,7 @@ int enqueue_step(EngineImpl& e, int n_seq, int Kseq) {
   e.cur_rows = K;
   e.cur_seqs = n_seq;
   e.cur_k = Kseq;
+  e.rp_idx = 0;  // two row-parallel matmuls a layer: every step starts on buffer 0
   const int32_t* tokens = n_seq ? e.d_bin + e.max_seqs : e.d_in->tokens;
   {
     Recorder rec(e, "embed", 4.0 * K * d.hidden);
@@ -1064,6 +1141,78 @@ extern "C" int iam_tp_shard_of(const iam_dims* dims, int rank, int world, iam_tp
 extern "C" int iam_nccl_unique_id(void* id128) { return iam::nccl_unique_id(id128); }
 
 static int comm_timeout_ms(const iam::EngineImpl& e) { return e.d.comm_timeout_ms > 0 ? e.d.comm_timeout_ms : 120000; }
+static int sync_step(iam::EngineImpl& e, const char* what);
+
+// Maps every rank's receive area for the row-parallel sums into every rank
+// (CUDA IPC; the handles travel through the communicator, and so do the
+// verdicts: either every rank could map every peer and all use the
+// peer-memory sums, or none does and the NCCL all-reduce stays).
+// IAM_TP_P2P=0 keeps the NCCL all-reduce.
+static int tp_p2p_init(iam::EngineImpl& e) {
+  using namespace iam;
+  const char* env = std::getenv("IAM_TP_P2P");
+  const bool want = !(env && env[0] == '0') && e.world <= kQmmMaxPeers;
+  const size_t R = static_cast<size_t>(e.d.max_rows), H = static_cast<size_t>(e.d.hidden);
+  e.tp_tiles = ceil_div(e.d.hidden, kQpRows);
+  e.tp_ctr_off = (2 * static_cast<size_t>(e.world) * R * H * sizeof(float) + 255) / 256 * 256;
+  const size_t bytes = e.tp_ctr_off + 2 * static_cast<size_t>(e.tp_tiles) * sizeof(int);
+  constexpr int kW = 9;  // a rank's words: its 64-byte handle and a verdict
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  bool ok = want;
+  cudaIpcMemHandle_t h{};
+  if (ok && (cudaMalloc(&e.tp_area, bytes) != cudaSuccess || cudaMemsetAsync(e.tp_area, 0, bytes, e.stream) != cudaSuccess ||
+             cudaIpcGetMemHandle(&h, e.tp_area) != cudaSuccess)) {
+    cudaGetLastError();
+    ok = false;
+  }
+  std::vector<unsigned long long> hx(static_cast<size_t>(e.world) * kW, 0ull);
+  std::memcpy(&hx[static_cast<size_t>(e.rank) * kW], &h, sizeof(h));
+  hx[static_cast<size_t>(e.rank) * kW + 8] = ok ? 1ull : 0ull;
+  unsigned long long* dx = nullptr;
+  E_CUDA(cudaMalloc(&dx, hx.size() * sizeof(unsigned long long)));
+  auto gather = [&]() -> int {
+    E_CUDA(cudaMemcpyAsync(dx, hx.data(), hx.size() * 8, cudaMemcpyHostToDevice, e.stream));
+    unsigned long long* mine = dx + static_cast<size_t>(e.rank) * kW;
+    E_RUN(nccl_allgather_u64(e.comm, mine, dx, kW, e.stream));
+    E_RUN(sync_step(e, "iam_create: exchanging peer-memory handles"));
+    E_CUDA(cudaMemcpy(hx.data(), dx, hx.size() * 8, cudaMemcpyDeviceToHost));
+    return IAM_OK;
+  };
+  int r = gather();
+  bool all = r == IAM_OK;
+  for (int q = 0; all && q < e.world; ++q) all = hx[static_cast<size_t>(q) * kW + 8] == 1ull;
+  if (all) {
+    for (int q = 0; q < e.world; ++q) {
+      if (q == e.rank) {
+        e.tp_peer[q] = e.tp_area;
+        continue;
+      }
+      cudaIpcMemHandle_t ph;
+      std::memcpy(&ph, &hx[static_cast<size_t>(q) * kW], sizeof(ph));
+      void* p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, ph, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        ok = false;
+        break;
+      }
+      e.tp_peer[q] = static_cast<char*>(p);
+    }
+    hx[static_cast<size_t>(e.rank) * kW + 8] = ok ? 1ull : 0ull;
+    r = gather();
+    for (int q = 0; r == IAM_OK && q < e.world; ++q) all = all && hx[static_cast<size_t>(q) * kW + 8] == 1ull;
+    all = all && r == IAM_OK;
+  }
+  cudaFree(dx);
+  if (!all) {
+    for (int q = 0; q < e.world; ++q)
+      if (q != e.rank && e.tp_peer[q]) cudaIpcCloseMemHandle(e.tp_peer[q]);
+    for (char*& p : e.tp_peer) p = nullptr;
+    if (e.tp_area) cudaFree(e.tp_area);
+    e.tp_area = nullptr;
+  }
+  e.tp_p2p = all;
+  return r;
+}
 
 extern "C" int iam_create(const iam_dims* dims, int device, int rank, int world, const void* nccl_id,
                           iam_engine** out) {
@@ -1093,6 +1242,7 @@ extern "C" int iam_create(const iam_dims* dims, int device, int rank, int world,
   if (r == IAM_OK) r = attn_init_attrs();
   if (r == IAM_OK) r = alloc_all(e);
   if (r == IAM_OK && world > 1) r = nccl_init(&e.comm, nccl_id, rank, world, comm_timeout_ms(e));
+  if (r == IAM_OK && world > 1) r = tp_p2p_init(e);
   if (r != IAM_OK) {
     iam_destroy(eng);
     return r;
@@ -1111,6 +1261,9 @@ extern "C" void iam_destroy(iam_engine* eng) {
   for (auto& kv : e.bgraphs) cudaGraphExecDestroy(kv.second);
   e.bgraphs.clear();
   if (e.comm) iam::nccl_destroy(e.comm);
+  for (int q = 0; q < e.world && q < iam::kQmmMaxPeers; ++q)
+    if (q != e.rank && e.tp_peer[q]) cudaIpcCloseMemHandle(e.tp_peer[q]);
+  if (e.tp_area) cudaFree(e.tp_area);
   void* bufs[] = {e.pool, e.ppool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
                   e.mid, e.mlp_h, e.q_buf, e.part_o, e.part_ml, e.red32, e.keys, e.best, e.rope_cs, e.d_in, e.d_out,
                   e.d_err, e.qws, e.qctr, e.gin, e.d_bin, e.d_bout};

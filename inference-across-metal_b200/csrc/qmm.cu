@@ -877,6 +877,9 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
   bool packed = a.seg[0].packed != nullptr;
   for (int i = 1; i < a.nseg; ++i)
     IAM_CHECK((a.seg[i].packed != nullptr) == packed, "qmm: segments mix packed and MLX-layout weights");
+  IAM_CHECK(a.npush >= 0 && a.npush <= kQmmMaxPeers, "qmm: 0..8 receive slots");
+  if (a.npush > 0)
+    IAM_CHECK(packed && a.nseg == 1 && a.seg[0].mode == EPI_F32, "qmm: pushing to peers needs one fp32 segment of packed weights");
   if (packed) {
     const int total_m = a.M;
     const uint16_t* x0 = a.x;
@@ -891,6 +894,7 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
         if (s.resid) s.resid += static_cast<size_t>(m0) * s.ldr;
         if (s.keys) s.keys += m0;
       }
+      for (int r = 0; r < p.npush; ++r) p.push[r] += static_cast<size_t>(m0) * a.seg[0].ldo;
       // narrow passes convert the weights in registers (mma.sync); wider ones
       // on the tensor cores
       const int r = p.M <= qmm_gemv_max_m() ? qmm_gemv_run(p, st, pdl, ws_floats_cap, ws_ctr_cap)
@@ -905,7 +909,7 @@ int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t w
     IAM_CHECK(aligned16(s.w), "qmm: w must be 16-byte aligned");
     if (s.mode == EPI_SWIGLU) IAM_CHECK(s.w2 && s.s2 && s.b2 && aligned16(s.w2), "qmm: SwiGLU needs the up matrix");
     if (s.mode == EPI_ARGMAX) IAM_CHECK(s.keys != nullptr && s.key_ld >= 1, "qmm: argmax needs a key buffer");
-    else if (s.mode == EPI_F32) IAM_CHECK(s.out32 != nullptr, "qmm: no fp32 output");
+    else if (s.mode == EPI_F32) IAM_CHECK(s.out32 != nullptr || a.npush > 0, "qmm: no fp32 output");
     else IAM_CHECK(s.out != nullptr, "qmm: no output");
     if (s.mode == EPI_RESID) IAM_CHECK(s.resid != nullptr, "qmm: residual input missing");
   }

@@ -35,6 +35,7 @@ struct QmmSeg {
 };
 
 constexpr int kQmmMaxSeg = 4;
+constexpr int kQmmMaxPeers = 8;
 
 struct QmmArgs {
   const uint16_t* x;  // x[tok * ldx + k], bf16
@@ -56,8 +57,33 @@ struct QmmArgs {
   // consumers' first wait is on a phase that nothing completes and must run
   // out (nothing is in flight when the CTA exits).
   int starve;
+  // Row-parallel matmul across GPUs (packed weights, one EPI_F32 segment):
+  // each tile's final fp32 values go to push[r] + tok * ldo + col for every
+  // rank r (this GPU's own slot and the peers' receive slots, by plain stores
+  // over NVLink), then one release add of 1 at system scope to push_ctr[r][tile]
+  // tells rank r that this rank's tile of the pass has landed.  npush = 0: the
+  // values go to out32.
+  int npush;
+  float* push[kQmmMaxPeers];
+  int* push_ctr[kQmmMaxPeers];
   QmmSeg seg[kQmmMaxSeg];
 };
+
+// Passes the packed-weight matmul makes over M tokens (64 tokens at most each).
+inline int qmm_packed_passes(int M) { return (M + 63) / 64; }
+
+// After a tile's values went out (all epilogue threads past a barrier): one
+// thread orders them before the arrivals at system scope and adds the
+// arrivals (cumulative through the barrier, so it publishes every thread's
+// stores to the peers).
+__device__ __forceinline__ void qmm_push_arrive(const QmmArgs& A, int tile) {
+  __threadfence_system();
+#pragma unroll
+  for (int r = 0; r < kQmmMaxPeers; ++r) {
+    if (r >= A.npush) break;
+    asm volatile("red.release.sys.global.add.s32 [%0], 1;" ::"l"(A.push_ctr[r] + tile) : "memory");
+  }
+}
 
 // Tile configuration chosen by the host for a given shape.
 struct QmmConfig {

@@ -45,11 +45,10 @@
 namespace iam {
 namespace {
 
-constexpr int kGvStages = 3;
-// Resident CTAs an SM: with 8-token passes three fit, so while a launch runs
-// two an SM the next kernel's CTAs can start early (programmatic dependent
-// launch) and prefetch their weights; 16-token passes fit two.
-__host__ __device__ constexpr int gv_min_ctas(int NT) { return NT == 1 ? 3 : 2; }
+constexpr int kGvStages = 4;
+// Resident CTAs an SM.  (Three, with a 3-stage ring at 72 registers, measured
+// slower on every shape: 248320 x 5120 at one token 170.9 against 152.7 us.)
+__host__ __device__ constexpr int gv_min_ctas(int) { return 2; }
 // QW: the number of consumer warps sharing one 32-row pair of a block, each
 // taking 4 / QW of its four 64-k groups; 4 QW consumer warps + 1 producer.
 __host__ __device__ constexpr int gv_warps(int QW) { return 4 * QW; }
@@ -427,6 +426,24 @@ __global__ void __launch_bounds__(gv_threads(QW), gv_min_ctas(NT)) qmm_gemv_kern
         for (int qq = 1; qq < 4; ++qq) k = kbuf[qq * TOK + ct] > k ? kbuf[qq * TOK + ct] : k;
         SG.keys[static_cast<size_t>(tile) * SG.key_ld + ct] = k;
       }
+    } else if (mode == EPI_F32 && A.npush > 0) {
+      // this rank's values of the tile into every rank's receive slot
+      const int grow = tile * kQpRows + row;
+      const size_t ldo = static_cast<size_t>(SG.ldo);
+      if (grow < SG.rows) {
+#pragma unroll
+        for (int r = 0; r < kQmmMaxPeers; ++r) {  // constant indices: the pointers straight from the parameters
+          if (r >= A.npush) break;
+          float* const dst = A.push[r];
+#pragma unroll
+          for (int j = 0; j < TPT; ++j) {
+            const int tok = tpar + QW * j;
+            if (tok < M) dst[tok * ldo + grow] = v[j];
+          }
+        }
+      }
+      named_bar_sync(2, kEpi);
+      if (ct == 0) qmm_push_arrive(A, tile);
     } else {
       const int grow = tile * kQpRows + row;
       uint16_t* const out = SG.out;
@@ -526,7 +543,7 @@ int qmm_gemv_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, siz
     QmmSeg& s = a.seg[i];
     IAM_CHECK(s.rows > 0 && s.packed && aligned16(s.packed), "qmm: segment without packed weights");
     if (s.mode == EPI_ARGMAX) IAM_CHECK(s.keys != nullptr && s.key_ld >= 1, "qmm: argmax needs a key buffer");
-    else if (s.mode == EPI_F32) IAM_CHECK(s.out32 != nullptr, "qmm: no fp32 output");
+    else if (s.mode == EPI_F32) IAM_CHECK(s.out32 != nullptr || a.npush > 0, "qmm: no fp32 output");
     else IAM_CHECK(s.out != nullptr, "qmm: no output");
     if (s.mode == EPI_RESID) IAM_CHECK(s.resid != nullptr, "qmm: residual input missing");
     s.cta_begin = cta;

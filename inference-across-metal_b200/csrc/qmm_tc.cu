@@ -484,6 +484,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
           for (int qq = 1; qq < 4; ++qq) k = kbuf[qq * NN + t] > k ? kbuf[qq * NN + t] : k;
           S.keys[static_cast<size_t>(tile) * S.key_ld + t] = k;
         }
+      } else if (mode == EPI_F32 && A.npush > 0) {
+        // this rank's values of the tile into every rank's receive slot
+        const int grow = tile * kQpRows + row;
+        const size_t ldo = static_cast<size_t>(S.ldo);
+        const int M = A.M;
+        if (grow < S.rows) {
+#pragma unroll
+          for (int r = 0; r < kQmmMaxPeers; ++r) {  // constant indices: the pointers straight from the parameters
+            if (r >= A.npush) break;
+            float* const dst = A.push[r];
+#pragma unroll
+            for (int e = 0; e < EC; ++e) {
+              const int tok = tok0 + e;
+              if (tok < M) dst[tok * ldo + grow] = v[e];
+            }
+          }
+        }
+        named_bar_sync(1, 32 * kTcDqWarps);
+        if (threadIdx.x == 64) qmm_push_arrive(A, tile);
       } else {
         const int grow = tile * kQpRows + row;
         // the fields in registers: the stores would make the compiler re-read
@@ -693,7 +712,7 @@ int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_
     QmmSeg& s = a.seg[i];
     IAM_CHECK(s.rows > 0 && s.packed && aligned16(s.packed), "qmm: segment without packed weights");
     if (s.mode == EPI_ARGMAX) IAM_CHECK(s.keys != nullptr && s.key_ld >= 1, "qmm: argmax needs a key buffer");
-    else if (s.mode == EPI_F32) IAM_CHECK(s.out32 != nullptr, "qmm: no fp32 output");
+    else if (s.mode == EPI_F32) IAM_CHECK(s.out32 != nullptr || a.npush > 0, "qmm: no fp32 output");
     else IAM_CHECK(s.out != nullptr, "qmm: no output");
     if (s.mode == EPI_RESID) IAM_CHECK(s.resid != nullptr, "qmm: residual input missing");
     s.cta_begin = cta;
