@@ -198,6 +198,8 @@ def run_gpu(args, rank, world, local_rank):
     ksteps = args.warmup + args.steps
     max_ctx = CTX + (ksteps + 2) * max(K, 1) * 2 + 64
     dims = I.Dims.qwen35_27b(max_ctx=max_ctx, max_rows=max(32, K))
+    if args.resident_gb:
+        dims.resident_weight_bytes = int(args.resident_gb * 1e9)
     nccl_id = None
     if world > 1:
         obj = [I.nccl_unique_id() if rank == 0 else None]
@@ -279,6 +281,7 @@ def run_gpu(args, rank, world, local_rank):
     prof = eng.profile_step(K, CTX)
     launches = eng.step_launches(K)
     step_bytes = eng.step_bytes(K, CTX)
+    n_streamed = eng.streamed_layers()
     hbm, peak_kind = peaks()
     q = prof.get("qmm", {"ms": 0.0, "bytes": 0.0, "launches": 1})
     q_gbs = q["bytes"] / (q["ms"] / 1000.0) / 1e9 if q["ms"] > 0 else 0.0
@@ -300,7 +303,8 @@ def run_gpu(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": bench_config(K, world),
+        "config": dict(bench_config(K, world), **({"resident_weight_gb": args.resident_gb,
+                                                    "streamed_layers": n_streamed} if args.resident_gb else {})),
         "k1": {"value": 1000.0 / ms1, "unit": "tokens/s", "ms_per_step": ms1},
         "hbm_roofline_step": {"bytes_per_step_per_gpu": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": hbm,
                               "frac": step_gbs / hbm, "peak_kind": peak_kind},
@@ -644,6 +648,8 @@ def main():
     ap.add_argument("--qmm-ms", default="1,2,4,8,16,32", help="token counts of --qmm-sweep")
     ap.add_argument("--batch", type=int, default=0, help="sequences of a multi-sequence verify step (with --k)")
     ap.add_argument("--ctx", type=int, default=4096, help="prior KV tokens per sequence of --batch")
+    ap.add_argument("--resident-gb", type=float, default=0.0,
+                    help="HBM budget (GB) for the layers' 4-bit matrices; the rest stream from pinned host memory")
     args = ap.parse_args()
     if args.sweep:
         return sweep(args)

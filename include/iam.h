@@ -235,6 +235,12 @@ typedef struct iam_dims {
   int comm_timeout_ms;   /* world > 1: bound on the communicator set-up and on each synchronous
                             step's wait for its collectives (0: 120000); past it the communicator
                             is aborted and the call returns IAM_ETIMEOUT */
+  long long resident_weight_bytes; /* HBM budget for the layers' 4-bit matrices, as loaded plus
+                            tile-packed (0: all resident).  Layers are kept resident in order
+                            while they fit; the 4-bit matrices of the rest live in pinned host
+                            memory and each step copies them, one layer ahead of its use, into
+                            two device slots on a second stream (the role of prefetchLayer,
+                            warm_forward.swift:556-650).  Outputs are bit-identical. */
 } iam_dims;
 
 /* Qwen3.5-27B defaults (full_forward.swift:18-49). */
@@ -397,6 +403,9 @@ int iam_profile_step(iam_engine* e, int K, int pos, int cap, const char** kinds,
                      int* launches);
 /* Number of kernel launches in one graph step of width K. */
 int iam_step_launches(iam_engine* e, int K);
+/* Layers whose 4-bit matrices stream from pinned host memory each step
+ * (dims.resident_weight_bytes), 0 when every layer is resident. */
+int iam_streamed_layers(const iam_engine* e);
 /* Algorithmic HBM bytes of one step of width K at position pos (weights +
  * state read/write + KV read), per GPU. */
 double iam_step_bytes(iam_engine* e, int K, int pos);

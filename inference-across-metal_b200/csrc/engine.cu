@@ -63,6 +63,8 @@ struct TensorRec {
   void* ptr = nullptr;
   int syn_kind;
   float p0 = 0.f, p1 = 0.f;
+  int layer = -1;     // decoder layer the tensor belongs to (-1: embedding, final norm, lm_head)
+  bool host = false;  // in pinned host memory (a 4-bit matrix of a streamed layer)
   size_t bytes() const { return static_cast<size_t>(shard.local_rows()) * (shard.col1 - shard.col0) * esize; }
 };
 
@@ -77,6 +79,12 @@ struct QW {
 struct Layer {
   bool attn = false;
   int idx = 0;  // index among GDN or among attention layers
+  // Streamed layers (beyond the resident budget): index among them (-1:
+  // resident), and where their packed matrices sit in the pinned host copy;
+  // the QW::packed pointers of a streamed layer point into device slot
+  // stream_j % 2.
+  int stream_j = -1;
+  size_t hp_off = 0, hp_bytes = 0;
   uint16_t* in_norm = nullptr;
   uint16_t* post_norm = nullptr;
   QW gate, up, down;
@@ -128,6 +136,21 @@ struct EngineImpl {
   // tensor was loaded or generated since the last pack.
   char* ppool = nullptr;
   size_t ppool_bytes = 0;
+  // Layers past dims.resident_weight_bytes: their 4-bit matrices as loaded
+  // (hpool) and tile-packed (hpacked) in pinned, device-mapped host memory;
+  // two device slots take turns holding one streamed layer's packed matrices,
+  // filled one layer ahead by copies on pf_stream (pf_ready[s]: slot s holds
+  // its next layer; pf_free[s]: the layer in slot s has finished).
+  char* hpool = nullptr;
+  char* hpacked = nullptr;
+  size_t hpool_bytes = 0, hpacked_bytes = 0;
+  char* slot[2] = {nullptr, nullptr};
+  size_t slot_bytes = 0;
+  int n_streamed = 0;
+  std::vector<int> streamed;  // layer index of each streamed layer, in order
+  cudaStream_t pf_stream = nullptr;
+  cudaEvent_t pf_ready[2] = {nullptr, nullptr}, pf_free[2] = {nullptr, nullptr}, pf_start = nullptr;
+  int reg_layer = -1;  // the layer build_registry is adding tensors for
   bool packed_dirty = true;
 
   std::vector<Layer> layers;
@@ -250,6 +273,7 @@ void add(EngineImpl& e, const std::string& name, const std::string& gen, Kind ki
   t.syn_kind = syn;
   t.p0 = p0;
   t.p1 = p1;
+  t.layer = e.reg_layer;
   e.by_name[name] = static_cast<int>(e.tensors.size());
   e.tensors.push_back(t);
 }
@@ -327,6 +351,7 @@ int build_registry(EngineImpl& e) {
   for (int li = 0; li < d.n_layers; ++li) {
     const std::string p = "model.layers." + std::to_string(li) + ".";
     const bool attn = (li + 1) % d.full_attn_interval == 0;
+    e.reg_layer = li;
     add(e, p + "input_layernorm.weight", p + "input_layernorm.weight", Kind::kBf16, 1, H, all,
         SYN_ONE_PLUS_NORMAL_BF16, 0.02f);
     if (attn) {
@@ -359,27 +384,163 @@ int build_registry(EngineImpl& e) {
     add_q4(e, p + "mlp.up_proj", I, H, rows_of(e.i0, e.i0 + e.inter_l), 0, 0);
     add_q4(e, p + "mlp.down_proj", H, I, all, e.i0, e.i0 + e.inter_l);
   }
+  e.reg_layer = -1;
+  return IAM_OK;
+}
+
+bool is_q4(const TensorRec& t) {
+  return t.kind == Kind::kQ4Words || t.kind == Kind::kQ4Scales || t.kind == Kind::kQ4Biases;
+}
+size_t aligned(size_t b) { return (b + kAlign - 1) / kAlign * kAlign; }
+
+// Output rows and K of every 4-bit matrix of layer li (pointers come later).
+void shape_layer(EngineImpl& e, Layer& L, int li) {
+  const iam_dims& d = e.d;
+  const int H = d.hidden;
+  L.attn = (li + 1) % d.full_attn_interval == 0;
+  auto sh = [](QW& q, int rows, int cols) {
+    q.rows = rows;
+    q.cols = cols;
+  };
+  sh(L.gate, e.inter_l, H);
+  sh(L.up, e.inter_l, H);
+  sh(L.down, H, e.inter_l);
+  if (L.attn) {
+    sh(L.q, 2 * e.hq_l * d.head_dim, H);
+    sh(L.k, e.hkv_l * d.head_dim, H);
+    sh(L.v, e.hkv_l * d.head_dim, H);
+    sh(L.o, H, e.hq_l * d.head_dim);
+  } else {
+    sh(L.qkv, e.conv_l, H);
+    sh(L.z, e.vd_l, H);
+    sh(L.bproj, e.gv_l, H);
+    sh(L.aproj, e.gv_l, H);
+    sh(L.out, H, e.vd_l);
+  }
+}
+
+// The packed matrices of a layer with their sizes, in their order inside the
+// packed pool (or inside a slot, for a streamed layer).
+std::vector<std::pair<unsigned char**, size_t>> layer_packed(EngineImpl& e, Layer& L) {
+  std::vector<std::pair<unsigned char**, size_t>> v;
+  auto need = [&](unsigned char** dst, int rows, int K, bool swiglu) {
+    v.push_back({dst, aligned(qp_bytes(qp_tiles(rows, swiglu), K))});
+  };
+  need(&L.gateup, e.inter_l, e.d.hidden, true);
+  need(&L.down.packed, L.down.rows, L.down.cols, false);
+  for (QW* q : {&L.q, &L.k, &L.v, &L.o, &L.qkv, &L.z, &L.bproj, &L.aproj, &L.out})
+    if (q->rows > 0) need(&q->packed, q->rows, q->cols, false);
+  return v;
+}
+
+// Which layers stream: in order, each stays resident while its 4-bit
+// matrices (as loaded and packed) fit in what is left of the budget.
+void plan_streaming(EngineImpl& e) {
+  const long long budget = e.d.resident_weight_bytes;
+  std::vector<size_t> bytes(e.layers.size(), 0);
+  for (const TensorRec& t : e.tensors)
+    if (t.layer >= 0 && is_q4(t)) bytes[t.layer] += aligned(t.bytes());
+  for (size_t li = 0; li < e.layers.size(); ++li)
+    for (auto& m : layer_packed(e, e.layers[li])) bytes[li] += m.second;
+  size_t used = 0;
+  bool streaming = false;
+  for (size_t li = 0; li < e.layers.size(); ++li) {
+    Layer& L = e.layers[li];
+    if (budget > 0 && (streaming || used + bytes[li] > static_cast<size_t>(budget))) {
+      streaming = true;
+      L.stream_j = e.n_streamed++;
+      e.streamed.push_back(static_cast<int>(li));
+    } else {
+      used += bytes[li];
+    }
+  }
+  for (TensorRec& t : e.tensors) t.host = t.layer >= 0 && is_q4(t) && e.layers[t.layer].stream_j >= 0;
+}
+
+// Packed copies: the resident layers' matrices and the lm_head in one device
+// pool, every matrix at a 256-byte boundary with zero padding; a streamed
+// layer's matrices at the same offsets inside device slot stream_j % 2, and
+// layer after layer in the pinned host copy.
+int alloc_packed(EngineImpl& e) {
+  std::vector<std::pair<unsigned char**, size_t>> want;
+  for (Layer& L : e.layers) {
+    auto v = layer_packed(e, L);
+    if (L.stream_j < 0) {
+      want.insert(want.end(), v.begin(), v.end());
+      continue;
+    }
+    size_t tot = 0;
+    for (auto& m : v) tot += m.second;
+    L.hp_off = e.hpacked_bytes;
+    L.hp_bytes = tot;
+    e.hpacked_bytes += tot;
+    e.slot_bytes = std::max(e.slot_bytes, tot);
+  }
+  want.push_back({&e.lm.packed, aligned(qp_bytes(qp_tiles(e.lm.rows, false), e.lm.cols))});
+  size_t tot = 0;
+  for (auto& w : want) tot += w.second;
+  E_CUDA(cudaMalloc(&e.ppool, std::max<size_t>(tot, 256)));
+  E_CUDA(cudaMemset(e.ppool, 0, std::max<size_t>(tot, 256)));
+  e.ppool_bytes = tot;
+  size_t off = 0;
+  for (auto& w : want) {
+    *w.first = reinterpret_cast<unsigned char*>(e.ppool + off);
+    off += w.second;
+  }
+  if (e.n_streamed == 0) return IAM_OK;
+  for (int s = 0; s < 2; ++s) {
+    E_CUDA(cudaMalloc(&e.slot[s], e.slot_bytes));
+    E_CUDA(cudaMemset(e.slot[s], 0, e.slot_bytes));
+    E_CUDA(cudaEventCreateWithFlags(&e.pf_ready[s], cudaEventDisableTiming));
+    E_CUDA(cudaEventCreateWithFlags(&e.pf_free[s], cudaEventDisableTiming));
+  }
+  E_CUDA(cudaEventCreateWithFlags(&e.pf_start, cudaEventDisableTiming));
+  E_CUDA(cudaHostAlloc(&e.hpacked, e.hpacked_bytes, cudaHostAllocPortable));
+  E_CUDA(cudaStreamCreateWithFlags(&e.pf_stream, cudaStreamNonBlocking));
+  for (Layer& L : e.layers) {
+    if (L.stream_j < 0) continue;
+    size_t o = 0;
+    for (auto& m : layer_packed(e, L)) {
+      *m.first = reinterpret_cast<unsigned char*>(e.slot[L.stream_j % 2] + o);
+      o += m.second;
+    }
+  }
   return IAM_OK;
 }
 
 int alloc_all(EngineImpl& e) {
   const iam_dims& d = e.d;
-  size_t total = 0;
-  for (auto& t : e.tensors) total += (t.bytes() + kAlign - 1) / kAlign * kAlign;
-  e.pool_bytes = total;
-  E_CUDA(cudaMalloc(&e.pool, total));
-  size_t off = 0;
+  e.layers.resize(d.n_layers);
+  for (int li = 0; li < d.n_layers; ++li) shape_layer(e, e.layers[li], li);
+  plan_streaming(e);
+  size_t dev_total = 0, host_total = 0;
+  for (auto& t : e.tensors) (t.host ? host_total : dev_total) += aligned(t.bytes());
+  e.pool_bytes = dev_total;
+  E_CUDA(cudaMalloc(&e.pool, std::max<size_t>(dev_total, 256)));
+  if (host_total) {
+    // pinned and mapped: the generator and pack kernels read and write it in
+    // place, through the same address (unified addressing)
+    E_CUDA(cudaHostAlloc(&e.hpool, host_total, cudaHostAllocMapped | cudaHostAllocPortable));
+    e.hpool_bytes = host_total;
+    void* dp = nullptr;
+    E_CUDA(cudaHostGetDevicePointer(&dp, e.hpool, 0));
+    if (dp != e.hpool) return e.setf(IAM_ECUDA, "streamed weights need unified addressing of pinned host memory");
+  }
+  size_t off = 0, hoff = 0;
   for (auto& t : e.tensors) {
-    t.ptr = e.pool + off;
-    off += (t.bytes() + kAlign - 1) / kAlign * kAlign;
+    if (t.host) {
+      t.ptr = e.hpool + hoff;
+      hoff += aligned(t.bytes());
+    } else {
+      t.ptr = e.pool + off;
+      off += aligned(t.bytes());
+    }
   }
   // layers
-  e.layers.resize(d.n_layers);
   const int H = d.hidden;
   for (int li = 0; li < d.n_layers; ++li) {
     const std::string p = "model.layers." + std::to_string(li) + ".";
     Layer& L = e.layers[li];
-    L.attn = (li + 1) % d.full_attn_interval == 0;
     L.idx = L.attn ? e.n_attn++ : e.n_gdn++;
     L.in_norm = static_cast<uint16_t*>(tptr(e, p + "input_layernorm.weight"));
     L.post_norm = static_cast<uint16_t*>(tptr(e, p + "post_attention_layernorm.weight"));
@@ -408,32 +569,7 @@ int alloc_all(EngineImpl& e) {
   e.embed = static_cast<uint16_t*>(tptr(e, "model.embed_tokens.weight"));
   e.final_norm = static_cast<uint16_t*>(tptr(e, "model.norm.weight"));
   e.lm = qw(e, "lm_head", e.vocab_l, H);
-
-  // packed copies: one pool, every matrix at a 256-byte boundary, zero padding
-  {
-    std::vector<std::pair<unsigned char**, size_t>> want;
-    auto need = [&](unsigned char** dst, int rows, int K, bool swiglu) {
-      want.push_back({dst, (qp_bytes(qp_tiles(rows, swiglu), K) + kAlign - 1) / kAlign * kAlign});
-    };
-    for (Layer& L : e.layers) {
-      need(&L.gateup, e.inter_l, H, true);
-      need(&L.down.packed, L.down.rows, L.down.cols, false);
-      for (QW* q : {&L.q, &L.k, &L.v, &L.o, &L.qkv, &L.z, &L.bproj, &L.aproj, &L.out})
-        if (q->w) need(&q->packed, q->rows, q->cols, false);
-    }
-    need(&e.lm.packed, e.lm.rows, e.lm.cols, false);
-    size_t tot = 0;
-    for (auto& w : want) tot += w.second;
-    E_CUDA(cudaMalloc(&e.ppool, std::max<size_t>(tot, 256)));
-    E_CUDA(cudaMemset(e.ppool, 0, std::max<size_t>(tot, 256)));
-    e.ppool_bytes = tot;
-    size_t off = 0;
-    for (auto& w : want) {
-      *w.first = reinterpret_cast<unsigned char*>(e.ppool + off);
-      off += w.second;
-    }
-  }
-
+  E_RUN(alloc_packed(e));
   // state
   e.max_seqs = d.max_seqs;
   const size_t slots = static_cast<size_t>(e.max_seqs);
@@ -558,6 +694,9 @@ int ensure_packed(EngineImpl& e) {
     return r;
   };
   for (const Layer& L : e.layers) {
+    // a streamed layer is packed in its slot (cleared first: the slot held
+    // other matrices) and copied out to the pinned host copy
+    if (L.stream_j >= 0) E_CUDA(cudaMemsetAsync(e.slot[L.stream_j % 2], 0, L.hp_bytes, e.stream));
     const int gt = qp_tiles(e.inter_l, true);
     E_RUN(qmm_pack_begin(L.gateup, gt, L.gate.cols, e.stream));
     E_RUN(qmm_pack_scan(L.gate.s, L.gate.rows, L.gate.cols, L.gateup, gt, 64, e.stream));
@@ -567,6 +706,9 @@ int ensure_packed(EngineImpl& e) {
     E_RUN(pk(L.down));
     for (const QW* q : {&L.q, &L.k, &L.v, &L.o, &L.qkv, &L.z, &L.bproj, &L.aproj, &L.out})
       if (q->w) E_RUN(pk(*q));
+    if (L.stream_j >= 0)
+      E_CUDA(cudaMemcpyAsync(e.hpacked + L.hp_off, e.slot[L.stream_j % 2], L.hp_bytes, cudaMemcpyDeviceToHost,
+                             e.stream));
   }
   E_RUN(pk(e.lm));
   E_CUDA(cudaStreamSynchronize(e.stream));
@@ -921,6 +1063,17 @@ int enqueue_finish_seqs(EngineImpl& e, int nparts, int n_seq, int Kseq) {
   return IAM_OK;
 }
 
+// Copies streamed layer j's packed matrices into slot j % 2 on the prefetch
+// stream, once the layer that held the slot before it (j - 2) has finished.
+int prefetch_layer(EngineImpl& e, int j) {
+  const Layer& L = e.layers[e.streamed[j]];
+  const int s = j % 2;
+  if (j >= 2) E_CUDA(cudaStreamWaitEvent(e.pf_stream, e.pf_free[s], 0));
+  E_CUDA(cudaMemcpyAsync(e.slot[s], e.hpacked + L.hp_off, L.hp_bytes, cudaMemcpyHostToDevice, e.pf_stream));
+  E_CUDA(cudaEventRecord(e.pf_ready[s], e.pf_stream));
+  return IAM_OK;
+}
+
 // One step of the whole model: K rows of the single sequence (n_seq = 0), or
 // K rows of each of the sequences in slots 0..n_seq-1 (n_seq >= 1, the
 // multi-sequence step: inputs and outputs in d_bin / d_bout).
@@ -936,10 +1089,23 @@ int enqueue_step(EngineImpl& e, int n_seq, int Kseq) {
     Recorder rec(e, "embed", 4.0 * K * d.hidden);
     E_RUN(launch_embed_bf16(e.embed, tokens, e.hidden, K, d.hidden, d.vocab, e.d_err, e.stream, false));
   }
+  if (e.n_streamed) {
+    // the prefetch stream forks from the step's start (the slots are free:
+    // the previous step precedes it on the engine stream)
+    E_CUDA(cudaEventRecord(e.pf_start, e.stream));
+    E_CUDA(cudaStreamWaitEvent(e.pf_stream, e.pf_start, 0));
+    for (int j = 0; j < std::min(2, e.n_streamed); ++j) E_RUN(prefetch_layer(e, j));
+  }
   for (const Layer& L : e.layers) {
+    const int j = L.stream_j;
+    if (j >= 0) E_CUDA(cudaStreamWaitEvent(e.stream, e.pf_ready[j % 2], 0));
     if (L.attn) E_RUN(enqueue_attn(e, L, K));
     else E_RUN(enqueue_gdn(e, L, K));
     E_RUN(enqueue_mlp(e, L, K));
+    if (j >= 0) {
+      E_CUDA(cudaEventRecord(e.pf_free[j % 2], e.stream));
+      if (j + 2 < e.n_streamed) E_RUN(prefetch_layer(e, j + 2));
+    }
   }
   {
     Recorder rec(e, "rmsnorm", 4.0 * K * d.hidden);
@@ -1085,6 +1251,8 @@ extern "C" void iam_dims_qwen35_27b(iam_dims* d) {
   d->max_ctx = 4608;
   d->max_rows = 128;
   d->max_seqs = 1;
+  d->comm_timeout_ms = 0;
+  d->resident_weight_bytes = 0;
 }
 
 static int validate_dims(const iam_dims& d, int world) {
@@ -1264,6 +1432,16 @@ extern "C" void iam_destroy(iam_engine* eng) {
   for (int q = 0; q < e.world && q < iam::kQmmMaxPeers; ++q)
     if (q != e.rank && e.tp_peer[q]) cudaIpcCloseMemHandle(e.tp_peer[q]);
   if (e.tp_area) cudaFree(e.tp_area);
+  if (e.pf_stream) cudaStreamSynchronize(e.pf_stream);
+  for (int s = 0; s < 2; ++s) {
+    if (e.slot[s]) cudaFree(e.slot[s]);
+    if (e.pf_ready[s]) cudaEventDestroy(e.pf_ready[s]);
+    if (e.pf_free[s]) cudaEventDestroy(e.pf_free[s]);
+  }
+  if (e.pf_start) cudaEventDestroy(e.pf_start);
+  if (e.pf_stream) cudaStreamDestroy(e.pf_stream);
+  if (e.hpool) cudaFreeHost(e.hpool);
+  if (e.hpacked) cudaFreeHost(e.hpacked);
   void* bufs[] = {e.pool, e.ppool, e.S, e.conv[0], e.conv[1], e.kc, e.vc, e.d_parity, e.hidden, e.resid, e.normed, e.inproj,
                   e.mid, e.mlp_h, e.q_buf, e.part_o, e.part_ml, e.red32, e.keys, e.best, e.rope_cs, e.d_in, e.d_out,
                   e.d_err, e.qws, e.qctr, e.gin, e.d_bin, e.d_bout};
@@ -1296,7 +1474,7 @@ extern "C" int iam_load_tensor(iam_engine* eng, const char* name, const void* ho
   for (auto& rr : t.shard.rows) {
     const size_t nrows = static_cast<size_t>(rr.second - rr.first);
     E_CUDA(cudaMemcpy2DAsync(dst, width, src + rr.first * pitch + t.shard.col0 * t.esize, pitch, width, nrows,
-                             cudaMemcpyHostToDevice, e.stream));
+                             cudaMemcpyDefault, e.stream));  // dst: device, or pinned host for a streamed layer
     dst += nrows * width;
   }
   E_CUDA(cudaStreamSynchronize(e.stream));
@@ -1446,7 +1624,7 @@ struct Staging {
     return cudaSuccess;
   }
   cudaError_t send(void* dst, size_t n) {
-    cudaError_t r = cudaMemcpyAsync(dst, buf[cur], n, cudaMemcpyHostToDevice, st);
+    cudaError_t r = cudaMemcpyAsync(dst, buf[cur], n, cudaMemcpyDefault, st);  // dst may be pinned host memory
     if (r == cudaSuccess) r = cudaEventRecord(ev[cur], st);
     return r;
   }
@@ -1622,7 +1800,7 @@ extern "C" int iam_read_tensor(iam_engine* eng, const char* name, void* host_ptr
   if (it != e.by_name.end()) {
     if (bytes > e.tensors[it->second].bytes())
       return e.setf(IAM_EINVAL, "iam_read_tensor: more bytes requested than the tensor holds");
-    E_CUDA(cudaMemcpy(host_ptr, e.tensors[it->second].ptr, bytes, cudaMemcpyDeviceToHost));
+    E_CUDA(cudaMemcpy(host_ptr, e.tensors[it->second].ptr, bytes, cudaMemcpyDefault));
     return IAM_OK;
   }
   const bool isS = n.rfind("state.S.", 0) == 0, isC = n.rfind("state.conv.", 0) == 0;
@@ -1903,6 +2081,8 @@ extern "C" int iam_verify_device(iam_engine* eng, const int32_t* d_tokens, int K
     return e.setf(IAM_EINVAL, "iam_verify_device: K out of range (1..max_rows, <= 256)");
   if (e.world > 1 && !e.comm) return e.setf(IAM_ESTATE, "iam_verify_device: the communicator was aborted");
   cudaStream_t st = stream ? as_stream(stream) : e.stream;
+  E_CUDA(cudaSetDevice(e.device));
+  E_RUN(ensure_packed(e));  // weights loaded or generated since the last step: pack them first
   cudaGraphExec_t g = nullptr;
   E_RUN(get_graph(e, K, &g));
   // pos < 0 keeps the device position (advanced by the previous step); the
@@ -2031,6 +2211,8 @@ extern "C" int iam_read_hidden(iam_engine* eng, uint16_t* host_ptr, int K) {
   E_CUDA(cudaMemcpy(host_ptr, e.normed, static_cast<size_t>(K) * e.d.hidden * 2, cudaMemcpyDeviceToHost));
   return IAM_OK;
 }
+
+extern "C" int iam_streamed_layers(const iam_engine* eng) { return eng ? eng->impl.n_streamed : -1; }
 
 extern "C" int iam_step_launches(iam_engine* eng, int K) {
   if (!eng) return -1;

@@ -71,6 +71,7 @@ _SIGS = {
     "iam_read_hidden": (_i, [_vp, _vp, _i]),
     "iam_profile_step": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "iam_step_launches": (_i, [_vp, _i]),
+    "iam_streamed_layers": (_i, [_vp]),
     "iam_step_bytes": (C.c_double, [_vp, _i, _i]),
     "iam_step_bytes_batch": (C.c_double, [_vp, _i, _i, _i]),
     "iam_verify_batch": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
@@ -218,7 +219,7 @@ class Dims(C.Structure):
     _fields_ = [(n, C.c_float if n in ("rope_theta", "eps") else C.c_int) for n in (
         "hidden", "intermediate", "vocab", "n_layers", "full_attn_interval", "n_heads", "n_kv_heads", "head_dim",
         "rotary_dim", "rope_theta", "gdn_k_heads", "gdn_v_heads", "gdn_dk", "gdn_dv", "conv_kernel", "group_size",
-        "eps", "max_ctx", "max_rows", "max_seqs", "comm_timeout_ms")]
+        "eps", "max_ctx", "max_rows", "max_seqs", "comm_timeout_ms")] + [("resident_weight_bytes", C.c_longlong)]
 
     @classmethod
     def qwen35_27b(cls, **over):
@@ -378,6 +379,10 @@ class Engine:
         if got < 0:
             self._c(-got)
         return {kinds[i].decode(): {"ms": ms[i], "bytes": by[i], "launches": n[i]} for i in range(got)}
+
+    def streamed_layers(self) -> int:
+        """Layers whose 4-bit matrices stream from pinned host memory each step."""
+        return lib().iam_streamed_layers(self._h)
 
     def step_launches(self, K: int) -> int:
         return lib().iam_step_launches(self._h, K)

@@ -147,6 +147,36 @@ def test_tiny_model_verify(K):
     e.close()
 
 
+@pytest.mark.parametrize("K", [1, 5, 48])
+def test_device_resident_step_on_fresh_weights(K):
+    """iam_verify_device straight after the weights were generated (no host
+    step before it): the step packs the weights first, so its argmax, accept
+    length and hidden state equal the host-driven step's, bit for bit."""
+    d = O.TINY
+    tokens = SM.draft_tokens(SEED, d, K, tag=f"dev{K}")
+    pos = 20
+    got = []
+    for how in ("device", "host"):
+        e = I.Engine(cdims(d, 96, 64))
+        e.init_synthetic(SEED)
+        e.state_init(SEED, pos)
+        if how == "device":
+            dt = torch.tensor(np.asarray(tokens, np.int32), device="cuda")
+            out = torch.zeros(K, dtype=torch.int32, device="cuda")
+            e.verify_device(dt.data_ptr(), K, pos, out.data_ptr())
+            e.status()
+            am = out.cpu().numpy().tolist()
+        else:
+            am, _ = e.verify(tokens, pos)
+            am = list(am)
+        got.append((am, e.read_hidden(K).copy()))
+        e.close()
+    assert got[0][0] == got[1][0]
+    assert np.array_equal(got[0][1], got[1][1])
+    W, st, am_ref, acc_ref, normed, logits = oracle_step(d, tokens, pos, pos, 96)
+    check_argmax(got[0][0], logits)
+
+
 def test_tiny_model_verify_wide_block():
     """K = 48: every matmul of the step (fused projections, SwiGLU, residual,
     lm_head argmax) on the tensor-core kernel's 64-token tile."""
