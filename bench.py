@@ -153,6 +153,53 @@ def oracle_sample(K: int, threads: int):
     return K / step, t3 - t0, desc
 
 
+def cpu_layers(threads: int, reps: int = 3) -> dict:
+    """The single-layer workloads at K = 1 on the CPU restatement (numpy fp32
+    with the multi-threaded C dequant, dequantisation included), median of
+    `reps`: one GDN layer at full size (its mixer alone is the layer minus the
+    MLP, timed on its own) and one attention + SwiGLU MLP layer at position
+    CTX - 1 over CTX - 1 prior KV rows."""
+    import numpy as np
+    from oracle import fast as F
+    from oracle import iam_oracle as O
+    from oracle import synth_model as SM
+    d = O.QWEN35_27B
+    W = F.make_layer(SEED, d, 0)
+    W.update(F.make_layer(SEED, d, 3))
+    st = SM.make_state(SEED, d, CTX - 1, CTX, layers=[0, 3])
+    x = SM.hidden_input(SEED, d, 1)
+    g, a, m = [], [], []
+    with F.fast_dequant():
+        for _ in range(reps):
+            conv, S = st.conv[0].copy(), st.S[0].copy()
+            t0 = time.perf_counter()
+            O.gdn_block(x, W, "model.layers.0.", conv, S, d)
+            t1 = time.perf_counter()
+            O.attn_block(x, W, "model.layers.3.", st.k_cache[3], st.v_cache[3], CTX - 1, d)
+            t2 = time.perf_counter()
+            O.mlp(O.rms_norm(x, W["model.layers.3.post_attention_layernorm.weight"], d.eps), W, "model.layers.3.")
+            t3 = time.perf_counter()
+            g.append(t1 - t0)
+            a.append(t2 - t1)
+            m.append(t3 - t2)
+    med = statistics.median
+    return {"gdn_layer_ms": 1e3 * med(g), "gdn_mixer_ms": 1e3 * (med(g) - med(m)), "attn_mlp_layer_ms": 1e3 * med(a),
+            "threads": threads, "reps": reps,
+            "kind": "port: numpy fp32 oracle + C dequant (OpenMP), dequantisation included"}
+
+
+def gpu_layers(eng, K: int, pos: int) -> dict:
+    """Median device time of the GDN and attention layers of one eager step
+    (CUDA events around every launch; no overlap between launches)."""
+    lay = eng.profile_layers(K, pos)
+    med = statistics.median
+    gdn = [x for x in lay if not x[0]]
+    att = [x for x in lay if x[0]]
+    return {"gdn_mixer_us": 1e3 * med([x[1] for x in gdn]), "gdn_layer_us": 1e3 * med([x[1] + x[2] for x in gdn]),
+            "attn_mlp_layer_us": 1e3 * med([x[1] + x[2] for x in att]), "mlp_us": 1e3 * med([x[2] for x in lay]),
+            "layers": [len(gdn), len(att)], "timing": "eager step, CUDA events around every launch, median over layers"}
+
+
 def run_reference(args, rank, world):
     """The reference arm: the CPU restatement of the path (the reference's own
     implementation is Swift + Metal + a binary MLX kernel and cannot run here).
@@ -276,6 +323,10 @@ def run_gpu(args, rank, world, local_rank):
 
     # per-kernel-kind device time of one eager step (CUDA events on the engine stream)
     eng.state_init(SEED, CTX)
+    lay1 = gpu_layers(eng, 1, CTX - 1)
+    eng.state_init(SEED, CTX)
+    layK = gpu_layers(eng, K, CTX)
+    eng.state_init(SEED, CTX)
     prof1 = eng.profile_step(1, CTX)
     eng.state_init(SEED, CTX)
     prof = eng.profile_step(K, CTX)
@@ -315,6 +366,16 @@ def run_gpu(args, rank, world, local_rank):
                                      "traffic / weight-bytes ratio of one ncu capture (34816 x 5120, 32 tokens)",
                      "peak_kind": peak_kind, "launches_per_step": q["launches"], "ms_per_step": q["ms"],
                      "timing": "eager step, CUDA events on the engine stream around each launch"},
+        "layers": {
+            "gdn_layer_decode_k1": {"workload": "one GatedDeltaNet layer, K=1, 27B dims (the mixer: norm, fused "
+                                                "projections, conv + delta rule + gated norm, out_proj + residual)",
+                                    "gpu_us": lay1["gdn_mixer_us"], "gpu_us_with_mlp": lay1["gdn_layer_us"]},
+            "attn_mlp_layer_decode_k1": {"workload": "one full-attention layer + SwiGLU MLP, K=1, position 1023",
+                                         "gpu_us": lay1["attn_mlp_layer_us"]},
+            f"gdn_layer_verify_k{K}": {"gpu_us": layK["gdn_mixer_us"], "gpu_us_with_mlp": layK["gdn_layer_us"]},
+            f"attn_mlp_layer_verify_k{K}": {"gpu_us": layK["attn_mlp_layer_us"]},
+            "timing": lay1["timing"],
+        },
         "kernels_ms": {k: round(v["ms"], 4) for k, v in prof.items()},
         "kernels_ms_k1": {k: round(v["ms"], 4) for k, v in prof1.items()},
         "e2e": {"value": K / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * (K + 1),
@@ -324,6 +385,11 @@ def run_gpu(args, rank, world, local_rank):
         "prewarm_steps": n_pre,
     }
     if world == 1 and not args.no_cpu:
+        cl = cpu_layers(os.cpu_count() or 1)
+        line["layers"]["gdn_layer_decode_k1"]["cpu_ms_median3"] = cl["gdn_mixer_ms"]
+        line["layers"]["gdn_layer_decode_k1"]["cpu_ms_median3_with_mlp"] = cl["gdn_layer_ms"]
+        line["layers"]["attn_mlp_layer_decode_k1"]["cpu_ms_median3"] = cl["attn_mlp_layer_ms"]
+        line["layers"]["cpu"] = {"threads": cl["threads"], "reps": cl["reps"], "kind": cl["kind"]}
         v, secs, desc = oracle_sample(K, os.cpu_count() or 1)
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
                                 "sample": desc}

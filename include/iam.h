@@ -401,6 +401,12 @@ int iam_read_hidden(iam_engine* e, uint16_t* host_ptr, int K);
  * returns the number of kinds written (<= cap). */
 int iam_profile_step(iam_engine* e, int K, int pos, int cap, const char** kinds, double* ms, double* bytes,
                      int* launches);
+/* Device time of each decoder layer in one eager step of width K at pos
+ * (CUDA events around every launch, summed per layer): ms[i] for its
+ * attention or GDN block (input norm to the residual add), mlp_ms[i] for its
+ * MLP block, is_attn[i], for i < n_layers; returns n_layers (or minus a
+ * status). */
+int iam_profile_layers(iam_engine* e, int K, int pos, double* ms, double* mlp_ms, int* is_attn);
 /* Number of kernel launches in one graph step of width K. */
 int iam_step_launches(iam_engine* e, int K);
 /* Layers whose 4-bit matrices stream from pinned host memory each step

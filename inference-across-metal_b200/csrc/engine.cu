@@ -109,6 +109,7 @@ struct StepIn {  // device copy of the step inputs
 struct ProfEntry {
   std::string kind;
   double bytes;
+  int part;  // 2 * layer + (0: attention or GDN block, 1: MLP); -1: embedding, final norm, lm_head, finish
   cudaEvent_t a, b;
 };
 
@@ -223,6 +224,7 @@ struct EngineImpl {
   bool pdl = true;
   std::vector<ProfEntry>* prof = nullptr;
   int launches = 0;
+  int cur_part = -1;  // 2 * layer + block that enqueue_step is enqueuing (profiling tags)
 
   int setf(int st, const std::string& m) {
     err = m;
@@ -657,6 +659,7 @@ struct Recorder {
     e.launches++;
     if (e.prof) {
       ent.kind = k;
+      ent.part = e.cur_part;
       ent.bytes = b;
       cudaEventCreate(&ent.a);
       cudaEventCreate(&ent.b);
@@ -1098,15 +1101,18 @@ int enqueue_step(EngineImpl& e, int n_seq, int Kseq) {
   }
   for (const Layer& L : e.layers) {
     const int j = L.stream_j;
+    e.cur_part = 2 * static_cast<int>(&L - e.layers.data());
     if (j >= 0) E_CUDA(cudaStreamWaitEvent(e.stream, e.pf_ready[j % 2], 0));
     if (L.attn) E_RUN(enqueue_attn(e, L, K));
     else E_RUN(enqueue_gdn(e, L, K));
+    e.cur_part += 1;
     E_RUN(enqueue_mlp(e, L, K));
     if (j >= 0) {
       E_CUDA(cudaEventRecord(e.pf_free[j % 2], e.stream));
       if (j + 2 < e.n_streamed) E_RUN(prefetch_layer(e, j + 2));
     }
   }
+  e.cur_part = -1;
   {
     Recorder rec(e, "rmsnorm", 4.0 * K * d.hidden);
     E_RUN(launch_rms_norm(e.hidden, d.hidden, e.final_norm, e.normed, d.hidden, K, d.hidden, d.eps, e.stream, e.pdl));
@@ -2253,33 +2259,45 @@ extern "C" double iam_step_bytes_batch(iam_engine* eng, int n_seq, int K, int po
   return eng ? step_bytes(eng->impl, n_seq, K, pos) : 0.0;
 }
 
-extern "C" int iam_profile_step(iam_engine* eng, int K, int pos, int cap, const char** kinds, double* ms,
-                                double* bytes, int* launches) {
+// One eager (non-graph) step at width K with CUDA events around every launch.
+static int profile_run(iam_engine* eng, int K, int pos, std::vector<iam::ProfEntry>& ents) {
   using namespace iam;
   int r = verify_common(eng, K, pos);
-  if (r != IAM_OK) return -r;
+  if (r != IAM_OK) return r;
   EngineImpl& e = eng->impl;
-  static std::vector<std::string> names;
-  std::vector<ProfEntry> ents;
   e.h_in->pos = pos;
-  if (cudaMemcpyAsync(&e.d_in->pos, &e.h_in->pos, 4, cudaMemcpyHostToDevice, e.stream) != cudaSuccess) return -IAM_ECUDA;
+  E_CUDA(cudaMemcpyAsync(&e.d_in->pos, &e.h_in->pos, 4, cudaMemcpyHostToDevice, e.stream));
   e.prof = &ents;
   r = enqueue_step(e, 0, K);
   e.prof = nullptr;
+  if (r != IAM_OK) return r;
+  E_CUDA(cudaStreamSynchronize(e.stream));
+  return IAM_OK;
+}
+
+static float prof_ms(iam::ProfEntry& en) {
+  float x = 0.f;
+  cudaEventElapsedTime(&x, en.a, en.b);
+  cudaEventDestroy(en.a);
+  cudaEventDestroy(en.b);
+  return x;
+}
+
+extern "C" int iam_profile_step(iam_engine* eng, int K, int pos, int cap, const char** kinds, double* ms,
+                                double* bytes, int* launches) {
+  using namespace iam;
+  std::vector<ProfEntry> ents;
+  const int r = profile_run(eng, K, pos, ents);
   if (r != IAM_OK) return -r;
-  if (cudaStreamSynchronize(e.stream) != cudaSuccess) return -IAM_ECUDA;
+  static std::vector<std::string> names;
   std::vector<std::string> order;
   std::map<std::string, double> tms, tby;
   std::map<std::string, int> tn;
   for (auto& en : ents) {
-    float x = 0.f;
-    cudaEventElapsedTime(&x, en.a, en.b);
     if (!tn.count(en.kind)) order.push_back(en.kind);
-    tms[en.kind] += x;
+    tms[en.kind] += prof_ms(en);
     tby[en.kind] += en.bytes;
     tn[en.kind] += 1;
-    cudaEventDestroy(en.a);
-    cudaEventDestroy(en.b);
   }
   names = order;
   int n = 0;
@@ -2290,6 +2308,24 @@ extern "C" int iam_profile_step(iam_engine* eng, int K, int pos, int cap, const 
     bytes[n] = tby[k];
     launches[n] = tn[k];
     ++n;
+  }
+  return n;
+}
+
+extern "C" int iam_profile_layers(iam_engine* eng, int K, int pos, double* ms, double* mlp_ms, int* is_attn) {
+  using namespace iam;
+  std::vector<ProfEntry> ents;
+  const int r = profile_run(eng, K, pos, ents);
+  if (r != IAM_OK) return -r;
+  EngineImpl& e = eng->impl;
+  const int n = e.d.n_layers;
+  for (int i = 0; i < n; ++i) {
+    ms[i] = mlp_ms[i] = 0.0;
+    is_attn[i] = e.layers[i].attn ? 1 : 0;
+  }
+  for (auto& en : ents) {
+    const float x = prof_ms(en);
+    if (en.part >= 0 && en.part < 2 * n) (en.part & 1 ? mlp_ms : ms)[en.part >> 1] += x;
   }
   return n;
 }

@@ -72,6 +72,7 @@ _SIGS = {
     "iam_profile_step": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "iam_step_launches": (_i, [_vp, _i]),
     "iam_streamed_layers": (_i, [_vp]),
+    "iam_profile_layers": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "iam_step_bytes": (C.c_double, [_vp, _i, _i]),
     "iam_step_bytes_batch": (C.c_double, [_vp, _i, _i, _i]),
     "iam_verify_batch": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
@@ -379,6 +380,18 @@ class Engine:
         if got < 0:
             self._c(-got)
         return {kinds[i].decode(): {"ms": ms[i], "bytes": by[i], "launches": n[i]} for i in range(got)}
+
+    def profile_layers(self, K: int, pos: int):
+        """[(is_attention, block ms, MLP ms)] per decoder layer of one eager step
+        (CUDA events around every launch)."""
+        n = self.dims.n_layers
+        ms = (C.c_double * n)()
+        mm = (C.c_double * n)()
+        at = (C.c_int * n)()
+        got = lib().iam_profile_layers(self._h, K, pos, ms, mm, at)
+        if got < 0:
+            self._c(-got)
+        return [(bool(at[i]), ms[i], mm[i]) for i in range(got)]
 
     def streamed_layers(self) -> int:
         """Layers whose 4-bit matrices stream from pinned host memory each step."""
