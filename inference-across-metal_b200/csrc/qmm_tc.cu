@@ -288,10 +288,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // The warp runs the loop converged and one elected lane issues.  Each
-    // barrier check costs the issuing thread 100+ cycles while the tensor core
-    // needs only about 19 cycles an MMA at these shapes, so it synchronises
-    // once per 256-k block (16 MMAs): the block's activations and A slot.
+    // The warp runs the loop converged and one elected lane issues.  A barrier
+    // check costs the issuing warp a few hundred cycles, as much as the block's
+    // 16 MMAs, so it waits once per block, on the A slot only: the dequantizer
+    // warp that converts the block's first rows of its first half waits for
+    // the block's activations before it arrives on the slot.
     constexpr uint32_t idesc = umma_idesc_bf16(128, NN);
     const uint32_t dt = tmem + kTcDCol;
     bool ok = true;
@@ -299,8 +300,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     Ring<XS> xr;
     for (int i = 0; i < nkb; ++i, ar.next(), xr.next()) {
       const int slot = ar.idx, xsl = xr.idx;
-      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(xfull(xsl), xr.phase, abort_flag, lim) &&
-                                       mbar_wait_light(afull(slot), ar.phase, abort_flag, lim))) {
+      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(afull(slot), ar.phase, abort_flag, lim))) {
         ok = false;
         break;
       }
@@ -377,6 +377,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
       tmem_st8x4(lane_base + slot * 128 + (2 * gp + 1) * 32, r);
       tmem_wait_st();
       tc_fence_before();
+      // one warp of the team also vouches for the block's activations (the
+      // MMA issuer waits on the A slot alone)
+      if (q == 0 && gp == 0 &&
+          !__all_sync(0xffffffffu, mbar_wait_light(xfull(i % XS), static_cast<uint32_t>(i / XS) & 1u, abort_flag, lim))) {
+        give_up();
+        break;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(afull(slot));
     }
