@@ -247,6 +247,7 @@ def run_gpu(args, rank, world, local_rank):
     dims = I.Dims.qwen35_27b(max_ctx=max_ctx, max_rows=max(32, K))
     if args.resident_gb:
         dims.resident_weight_bytes = int(args.resident_gb * 1e9)
+    dims.comm_timeout_ms = 60000  # a peer that stops answering ends the run in a minute
     nccl_id = None
     if world > 1:
         obj = [I.nccl_unique_id() if rank == 0 else None]

@@ -922,15 +922,20 @@ __global__ void __launch_bounds__(512) tp_reduce_resid_kernel(const float* __res
   if (threadIdx.x == 0) {
     unsigned long long t0, t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    int v;
-    for (;;) {
+    int v = 0;
+    // after one wait gave up (a peer is gone), the rest of the step does not
+    // wait again: the step returns the error and the engine refuses further
+    // steps
+    bool failed = *reinterpret_cast<volatile int*>(err) == IAM_ETIMEOUT;
+    for (uint32_t n = 0; !failed; ++n) {
       asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr + tile) : "memory");
       if (v >= expect) break;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      if (t - t0 > limit_ns) break;
+      if (t - t0 > limit_ns) failed = true;
+      if ((n & 255) == 255 && *reinterpret_cast<volatile int*>(err) == IAM_ETIMEOUT) failed = true;
       __nanosleep(128);
     }
-    ok = v >= expect;
+    ok = !failed && v >= expect;
     if (ok) ctr[tile] = 0;
     else atomicCAS(err, 0, IAM_ETIMEOUT);
   }
@@ -1965,6 +1970,12 @@ static int device_status(iam::EngineImpl& e, const char* what) {
   *e.h_err = 0;
   E_CUDA(cudaMemsetAsync(e.d_err, 0, sizeof(int), e.stream));
   E_CUDA(cudaStreamSynchronize(e.stream));
+  if (st == IAM_ETIMEOUT && e.world > 1 && e.comm) {
+    // a peer-memory sum gave up: the ranks' arrival counters no longer agree,
+    // so the engine refuses further steps (like an aborted communicator)
+    nccl_abort(e.comm);
+    e.comm = nullptr;
+  }
   return e.setf(st, std::string(what) + ": device-side error " + iam_status_string(st) +
                         (st == IAM_ETIMEOUT ? " (a bounded wait inside a kernel gave up)" : ""));
 }

@@ -57,7 +57,9 @@ def _rank_main(rank, world, port):
 
             obj = [I.nccl_unique_id() if rank == 0 else None]
             dist.broadcast_object_list(obj, src=0)
-            e = I.Engine(cdims(d, ctx + 32, 8), device=rank, rank=rank, world=world, nccl_id=obj[0])
+            dims = cdims(d, ctx + 32, 8)
+            dims.comm_timeout_ms = 30000
+            e = I.Engine(dims, device=rank, rank=rank, world=world, nccl_id=obj[0])
             try:
                 e.init_synthetic(SEED)
                 e.state_init(SEED, ctx)
@@ -102,6 +104,7 @@ def _rank_batch(rank, world, port):
         dist.broadcast_object_list(obj, src=0)
         dims = cdims(d, ctx + 32, n * K)
         dims.max_seqs = n
+        dims.comm_timeout_ms = 30000
         e = I.Engine(dims, device=rank, rank=rank, world=world, nccl_id=obj[0])
         try:
             e.init_synthetic(SEED)
@@ -152,7 +155,9 @@ def _rank_p2p(rank, world, port):
                 os.environ["IAM_TP_P2P"] = "0"
             obj = [I.nccl_unique_id() if rank == 0 else None]
             dist.broadcast_object_list(obj, src=0)
-            e = I.Engine(cdims(d, ctx + 80, k), device=rank, rank=rank, world=world, nccl_id=obj[0])
+            dims = cdims(d, ctx + 80, k)
+            dims.comm_timeout_ms = 30000
+            e = I.Engine(dims, device=rank, rank=rank, world=world, nccl_id=obj[0])
             try:
                 e.init_synthetic(SEED)
                 e.state_init(SEED, ctx)
