@@ -196,33 +196,16 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   const uint16_t* conv_in = (swap ? a.conv_out : a.conv_in) + coff;
   uint16_t* conv_out = (swap ? const_cast<uint16_t*>(a.conv_in) : a.conv_out) + coff;
 
-  // conv channel of this thread: 0..127 q (K-head kh), 128..255 k, then this
-  // CTA's R v rows (V-head h)
-  const int ct = threadIdx.x;
-  int col = -1, region = -1, c = ct & 127;
-  if (ct < 128) {
-    col = kh * kHD + c;
-    region = 0;
-  } else if (ct < 256) {
-    col = a.key_dim + kh * kHD + c;
-    region = 1;
-  } else if (ct < 256 + R) {
-    c = jr * R + (ct - 256);
-    col = 2 * a.key_dim + h * kHD + c;
-    region = 2;
-  }
-  float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
-  uint16_t w0 = 0, w1 = 0, w2 = 0;  // window: the last three inputs (bf16)
-  if (col >= 0) {
-    const uint16_t* cw = a.conv_w + static_cast<size_t>(col) * 4;
-    k0 = bf2f(cw[0]);
-    k1 = bf2f(cw[1]);
-    k2 = bf2f(cw[2]);
-    k3 = bf2f(cw[3]);
-    w0 = conv_in[col];
-    w1 = conv_in[a.conv_dim + col];
-    w2 = conv_in[2 * a.conv_dim + col];
-  }
+  // The head's conv channels: 0..127 q (K-head kh), 128..255 k, then this
+  // CTA's R v rows (V-head h).  Global column of channel ci:
+  const int nch = 256 + R;
+  auto chan_col = [&](int ci) {
+    return ci < 128 ? kh * kHD + ci : ci < 256 ? a.key_dim + kh * kHD + (ci - 128) : 2 * a.key_dim + h * kHD + jr * R + (ci - 256);
+  };
+  // the conv input of global token u (u < 0: the window of the previous step)
+  auto conv_x = [&](int u, int col) -> uint16_t {
+    return u >= 0 ? in[static_cast<size_t>(u) * a.ld_in + col] : conv_in[static_cast<size_t>(3 + u) * a.conv_dim + col];
+  };
   // this lane's four gated-norm weights (phase D: lanes < R / 4)
   uint2 ww = make_uint2(0u, 0u);
   if (lane < R / 4) ww = *reinterpret_cast<const uint2*>(a.norm_w + jr * R + 4 * lane);
@@ -232,37 +215,32 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   int chunk = 0;
   for (int t0 = 0; t0 < a.rows; t0 += kChunk, ++chunk) {
     const int n = min(kChunk, a.rows - t0);
-    // ---- A: conv + SiLU for the chunk (depthwise_conv1d_m1_bf16, silu_bf16);
-    // all of the chunk's inputs are loaded before the sequential window
-    if (col >= 0) {
-      float* dst = region == 0 ? &sm.q[0][0] : region == 1 ? &sm.k[0][0] : &sm.v[0][0];
-      uint16_t xin[kChunk];
-#pragma unroll
-      for (int t = 0; t < kChunk; ++t)
-        xin[t] = t < n ? in[static_cast<size_t>(t0 + t) * a.ld_in + col] : uint16_t(0);
-#pragma unroll
-      for (int t = 0; t < kChunk; ++t) {
-        if (t < n) {
-          const uint16_t xi = xin[t];
-          float sum = 0.f;
-          sum = __fadd_rn(sum, __fmul_rn(bf2f(w0), k0));
-          sum = __fadd_rn(sum, __fmul_rn(bf2f(w1), k1));
-          sum = __fadd_rn(sum, __fmul_rn(bf2f(w2), k2));
-          sum = __fadd_rn(sum, __fmul_rn(bf2f(xi), k3));
-          dst[t * kHD + c] = round_bf(silu_f(round_bf(sum)));
-          w0 = w1;
-          w1 = w2;
-          w2 = xi;
-        }
-      }
-    } else if (ct >= 384 && ct - 384 < n) {
-      // ---- g, beta per token (compute_g_beta_bf16)
-      const int t = ct - 384;
+    // ---- A: conv + SiLU for the chunk (depthwise_conv1d_m1_bf16, silu_bf16),
+    // every (token, channel) pair independent: spread over all threads, each
+    // reading its four inputs (the tokens before the block from the window)
+    if (threadIdx.x < n) {
+      // g, beta per token (compute_g_beta_bf16)
+      const int t = threadIdx.x;
       const size_t row = static_cast<size_t>(t0 + t) * a.ld_in;
       float gv, bv;
       g_beta(bf2f(in[row + a.a_col + h]), bf2f(in[row + a.b_col + h]), a.A_log[h], bf2f(a.dt_bias[h]), gv, bv);
       sm.g[t] = gv;
       sm.beta[t] = bv;
+    }
+#pragma unroll 4
+    for (int idx = threadIdx.x; idx < n * nch; idx += kThreads) {
+      const int t = idx / nch, ci = idx - t * nch;
+      const int col = chan_col(ci);
+      const uint2 cw = *reinterpret_cast<const uint2*>(a.conv_w + static_cast<size_t>(col) * 4);
+      const int u = t0 + t;
+      const uint16_t x0 = conv_x(u - 3, col), x1 = conv_x(u - 2, col), x2 = conv_x(u - 1, col), x3 = conv_x(u, col);
+      float sum = 0.f;
+      sum = __fadd_rn(sum, __fmul_rn(bf2f(x0), lo_bf(cw.x)));
+      sum = __fadd_rn(sum, __fmul_rn(bf2f(x1), hi_bf(cw.x)));
+      sum = __fadd_rn(sum, __fmul_rn(bf2f(x2), lo_bf(cw.y)));
+      sum = __fadd_rn(sum, __fmul_rn(bf2f(x3), hi_bf(cw.y)));
+      float* dst = ci < 128 ? &sm.q[t][ci] : ci < 256 ? &sm.k[t][ci - 128] : &sm.v[t][jr * R + (ci - 256)];
+      *dst = round_bf(silu_f(round_bf(sum)));
     }
     __syncthreads();
     // ---- B: q^ = bf16(q_scale * (q / rms)), k^ likewise (per_head_rms_norm_scaled_bf16)
@@ -324,10 +302,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   store_state<RPW>(S, S_wr + hoff, row0, lane);
   // new conv state = the last three inputs; q/k channels are shared by the
   // `rep` V-heads of a K-head, the first CTA of the first of them writes them
-  if (col >= 0 && (region == 2 || (h % rep == 0 && jr == 0))) {
-    conv_out[col] = w0;
-    conv_out[a.conv_dim + col] = w1;
-    conv_out[2 * a.conv_dim + col] = w2;
+  if (threadIdx.x < nch && (threadIdx.x >= 256 || (h % rep == 0 && jr == 0))) {
+    const int col = chan_col(threadIdx.x);
+#pragma unroll
+    for (int j = 0; j < 3; ++j) conv_out[static_cast<size_t>(j) * a.conv_dim + col] = conv_x(a.rows - 3 + j, col);
   }
   if constexpr (C > 1) cluster_sync_all();  // no CTA leaves while a peer may read its shared memory
 }

@@ -50,7 +50,7 @@ namespace {
 // quadrant its SM sub-partition may access) and on 64-k group (w - 2) / 4 of
 // every 256-k block.
 constexpr int kTcDqWarps = 16;
-constexpr int kTcThreads = 32 * (2 + kTcDqWarps);
+constexpr int kTcThreads = 32 * (3 + kTcDqWarps);  // + a watcher warp (the last)
 constexpr int kTcASlots = 3;                         // TMEM A slots of one 256-k block (128 columns)
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcDCol = 128 * kTcASlots;        // accumulator: NN (<= 64) columns
@@ -288,11 +288,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // The warp runs the loop converged and one elected lane issues.  A barrier
-    // check costs the issuing warp a few hundred cycles, as much as the block's
-    // 16 MMAs, so it waits once per block, on the A slot only: the dequantizer
-    // warp that converts the block's first rows of its first half waits for
-    // the block's activations before it arrives on the slot.
+    // The warp runs the loop converged and one elected lane issues.  It never
+    // polls an mbarrier itself: the watcher warp waits for each block's A slot
+    // (the dequantizer warp converting the block's first rows of its first
+    // half also waited for the block's activations before arriving on it) and
+    // hands the block over through a named barrier.  (Barrier checks by the
+    // issuing warp cost about 400 cycles each even on a completed phase, as
+    // much as a block's 16 MMAs.)
     constexpr uint32_t idesc = umma_idesc_bf16(128, NN);
     const uint32_t dt = tmem + kTcDCol;
     bool ok = true;
@@ -300,7 +302,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     Ring<XS> xr;
     for (int i = 0; i < nkb; ++i, ar.next(), xr.next()) {
       const int slot = ar.idx, xsl = xr.idx;
-      if (!__all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(afull(slot), ar.phase, abort_flag, lim))) {
+      named_bar_sync(3, 64);  // with the watcher: block i is ready, or the CTA gave up
+      if (*abort_flag) {
         ok = false;
         break;
       }
@@ -323,6 +326,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     __syncwarp();
     // every MMA of this CTA has completed once dfull flips
     if (!__all_sync(0xffffffffu, mbar_wait(dfull, 0))) give_up();
+  } else if (warp == 2 + kTcDqWarps) {
+    // ------------------------------------------------------------ watcher
+    // Block by block: wait for the A slot, then meet the issuer (both sides
+    // meet once per block until one of them gives up).
+    Ring<kTcASlots> ar;
+    for (int i = 0; i < nkb; ++i, ar.next()) {
+      const bool got = __all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(afull(ar.idx), ar.phase, abort_flag, lim));
+      if (!got && lane == 0) give_up();
+      named_bar_sync(3, 64);
+      if (!got) break;
+    }
   } else {
     // ------------------------------------------------------------ dequantizers
     const int q = warp & 3, h = (warp - 2) >> 2;  // h: 64-k group of each block
@@ -706,6 +720,7 @@ static int tc_launch(const QmmTcArgs& ta, int ks, cudaStream_t st, bool pdl) {
 int qmm_tc_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap) {
   IAM_CHECK(a.K > 0 && a.K % 64 == 0, "qmm: K must be a positive multiple of 64");
   IAM_CHECK(a.M >= 1 && a.M <= 64, "qmm: the tensor-core path takes 1..64 tokens a pass");
+  IAM_CHECK(!a.norm_w, "qmm: the fused RMSNorm runs on the GEMV path only");
   IAM_CHECK(a.nseg >= 1 && a.nseg <= kQmmMaxSeg, "qmm: 1..4 segments");
   IAM_CHECK(aligned16(a.x) && a.ldx % 8 == 0 && a.ldx >= a.K, "qmm: x must be 16-byte aligned with ldx % 8 == 0");
   if (g_tc_sms == 0) {
