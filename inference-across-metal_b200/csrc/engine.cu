@@ -768,17 +768,36 @@ GdnArgs gdn_args(EngineImpl& e, const Layer& L, int rows, int n_seq) {
   return g;
 }
 
+// The RMSNorm ahead of a matmul over the residual stream: fused into the
+// matmul (its CTAs normalise the rows they read) when the step has at most
+// kGemvNormMaxM rows and runs on the GEMV path, which removes the norm
+// kernel's launch and its serialisation; else the norm kernel writes
+// e.normed.  Sets the matmul's input either way.  IAM_FUSED_NORM=0 keeps the
+// norm kernel.
+int norm_into(EngineImpl& e, QmmArgs& a, const uint16_t* x, const uint16_t* w, int K) {
+  const iam_dims& d = e.d;
+  const int H = d.hidden;
+  const char* env = std::getenv("IAM_FUSED_NORM");
+  const bool fuse = K <= kGemvNormMaxM && K <= qmm_gemv_max_m() && !(env && env[0] == '0');
+  a.ldx = H;
+  if (fuse) {
+    a.x = x;
+    a.norm_w = w;
+    a.norm_eps = d.eps;
+    return IAM_OK;
+  }
+  Recorder rec(e, "rmsnorm", 4.0 * K * H);
+  E_RUN(launch_rms_norm(x, H, w, e.normed, H, K, H, d.eps, e.stream, e.pdl));
+  a.x = e.normed;
+  return IAM_OK;
+}
+
 int enqueue_gdn(EngineImpl& e, const Layer& L, int K) {
   const iam_dims& d = e.d;
   const int H = d.hidden;
   uint16_t* const in = e.gin + static_cast<size_t>(L.idx) * d.max_rows * e.ld_in;
-  {
-    Recorder rec(e, "rmsnorm", 4.0 * K * H);
-    E_RUN(launch_rms_norm(e.hidden, H, L.in_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
-  }
   QmmArgs a = {};
-  a.x = e.normed;
-  a.ldx = H;
+  E_RUN(norm_into(e, a, e.hidden, L.in_norm, K));
   a.M = K;
   a.K = H;
   a.nseg = 4;
@@ -805,13 +824,8 @@ int enqueue_gdn(EngineImpl& e, const Layer& L, int K) {
 int enqueue_attn(EngineImpl& e, const Layer& L, int K) {
   const iam_dims& d = e.d;
   const int H = d.hidden, hd = d.head_dim;
-  {
-    Recorder rec(e, "rmsnorm", 4.0 * K * H);
-    E_RUN(launch_rms_norm(e.hidden, H, L.in_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
-  }
   QmmArgs a = {};
-  a.x = e.normed;
-  a.ldx = H;
+  E_RUN(norm_into(e, a, e.hidden, L.in_norm, K));
   a.M = K;
   a.K = H;
   a.nseg = 3;
@@ -876,13 +890,8 @@ int enqueue_attn(EngineImpl& e, const Layer& L, int K) {
 int enqueue_mlp(EngineImpl& e, const Layer& L, int K) {
   const iam_dims& d = e.d;
   const int H = d.hidden;
-  {
-    Recorder rec(e, "rmsnorm", 4.0 * K * H);
-    E_RUN(launch_rms_norm(e.resid, H, L.post_norm, e.normed, H, K, H, d.eps, e.stream, e.pdl));
-  }
   QmmArgs a = {};
-  a.x = e.normed;
-  a.ldx = H;
+  E_RUN(norm_into(e, a, e.resid, L.post_norm, K));
   a.M = K;
   a.K = H;
   a.nseg = 1;

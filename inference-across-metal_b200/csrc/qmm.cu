@@ -872,6 +872,10 @@ int qmm_op_workspace(int kind, size_t floats, size_t ctrs, cudaStream_t st, floa
 int qmm_run(QmmArgs a, cudaStream_t st, bool pdl, size_t ws_floats_cap, size_t ws_ctr_cap) {
   IAM_CHECK(a.K > 0 && a.K % 64 == 0, "qmm: K must be a positive multiple of 64");
   IAM_CHECK(a.M >= 1, "qmm: M must be >= 1");
+  if (a.norm_w)
+    IAM_CHECK(a.seg[0].packed && a.M <= kGemvNormMaxM && a.M <= qmm_gemv_max_m() && aligned16(a.norm_w) &&
+                  a.K % 256 == 0 && a.ldx % 8 == 0,
+              "qmm: the fused RMSNorm needs packed weights and at most two tokens on the GEMV path");
   IAM_CHECK(a.nseg >= 1 && a.nseg <= kQmmMaxSeg, "qmm: 1..4 segments");
   IAM_CHECK(aligned16(a.x) && a.ldx % 8 == 0, "qmm: x must be 16-byte aligned with ldx % 8 == 0");
   bool packed = a.seg[0].packed != nullptr;

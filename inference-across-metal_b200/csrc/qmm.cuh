@@ -66,8 +66,15 @@ struct QmmArgs {
   int npush;
   float* push[kQmmMaxPeers];
   int* push_ctr[kQmmMaxPeers];
+  // RMSNorm fused ahead of the matmul (GEMV passes of at most
+  // kGemvNormMaxM tokens): x holds the raw rows and the matmul's input is
+  // bf16((x / rms) * norm_w) with rms over each whole row, computed in the
+  // reference's summation order (rms_norm_bf16).  Null: x is the input.
+  const uint16_t* norm_w;
+  float norm_eps;
   QmmSeg seg[kQmmMaxSeg];
 };
+constexpr int kGemvNormMaxM = 2;
 
 // Passes the packed-weight matmul makes over M tokens (64 tokens at most each).
 inline int qmm_packed_passes(int M) { return (M + 63) / 64; }

@@ -39,6 +39,7 @@
 #include <type_traits>
 
 #include "kernels.cuh"
+#include "rmsnorm.cuh"
 #include "tc.cuh"
 #include "tma.cuh"
 
@@ -67,6 +68,8 @@ struct GvLayout {
   static constexpr int kNumBars = 2 * kGvStages;           // full[S], empty[S]
   // barriers, then abort / last flags (64 bytes), then this CTA's segment
   static constexpr int kSmem = kBarOff + kNumBars * 8 + 64 + 128 + 1024;  // + alignment slack
+  // the input rows the consumers build for a fused RMSNorm (runtime size, after the tail)
+  static constexpr int kNxOff = (kBarOff + kNumBars * 8 + 64 + 128 + 15) / 16 * 16;
   // after the block loop the ring holds the k parts' partials [QW][128][kTok]
   // fp32, the tile's sums [128][kTok] and the argmax keys [4][kTok]
   static constexpr int kRedBytes = 128 * kTok * 4;
@@ -174,13 +177,15 @@ __global__ void __launch_bounds__(gv_threads(QW), gv_min_ctas(NT)) qmm_gemv_kern
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const unsigned char* wsrc = SG.packed + (static_cast<size_t>(tile) * KB + kb0) * kQpBlockBytes;
+      const bool own_x = A.norm_w == nullptr;  // fused norm: the consumers build x themselves
       auto load_w = [&](int i) {
         const int s = i % S;
-        mbar_expect_tx(full(s), kQpBlockBytes + L::kXBytes);
+        mbar_expect_tx(full(s), kQpBlockBytes + (own_x ? L::kXBytes : 0));
         bulk_load(sbase + s * L::kStage + L::kXBytes, wsrc + static_cast<size_t>(i) * kQpBlockBytes, kQpBlockBytes,
                   full(s));
       };
       auto load_x = [&](int i) {
+        if (!own_x) return;
         const int s = i % S;
 #pragma unroll
         for (int b = 0; b < 4; ++b)
@@ -235,6 +240,38 @@ __global__ void __launch_bounds__(gv_threads(QW), gv_min_ctas(NT)) qmm_gemv_kern
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) xon[nt] = nt * 8 + g < M;
 
+  // Fused RMSNorm (rms_norm_bf16, full_forward.swift:59-86) ahead of the
+  // matmul: x holds the raw rows.  Warp t sums row t in the reference's order;
+  // then the consumers write bf16((x / rms) * w) for this CTA's blocks into
+  // shared memory in the layout the copies would have had (rows < M only,
+  // the boxes M rows apart), and the block loop reads it from there.
+  const bool norm = A.norm_w != nullptr;
+  unsigned char* const nx = smem + L::kNxOff;
+  const int nxbox = M * 128;
+  const int nxrow = GPW * qp * nxbox + g * 128;
+  if (norm) {
+    pdl_wait();  // the rows come from the preceding kernel
+    float* rms_s = reinterpret_cast<float*>(tail + 16);
+    if (warp < M) {
+      const uint4* xrow = reinterpret_cast<const uint4*>(A.x + static_cast<size_t>(warp) * A.ldx);
+      const float rms = rms_row_warp([&](int i) { return xrow[i]; }, A.K, A.norm_eps, lane);
+      if (lane == 0) rms_s[warp] = rms;
+    }
+    named_bar_sync(1, 32 * kGvWarps);
+    const int nchunk = nkb * 32;  // 8-element chunks of a row over this CTA's blocks
+    for (int idx = threadIdx.x; idx < M * nchunk; idx += 32 * kGvWarps) {
+      const int tr = idx / nchunk, kc = idx - tr * nchunk;
+      const int k = (kb0 * 32 + kc) * 8;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (k < A.K)
+        v = rms_apply8(*reinterpret_cast<const uint4*>(A.x + static_cast<size_t>(tr) * A.ldx + k),
+                       *reinterpret_cast<const uint4*>(A.norm_w + k), rms_s[tr]);
+      const int blk = kc >> 5, box = (kc >> 3) & 3, c = kc & 7;
+      *reinterpret_cast<uint4*>(nx + (blk * 4 + box) * nxbox + tr * 128 + ((c ^ (tr & 7)) << 4)) = v;
+    }
+    named_bar_sync(1, 32 * kGvWarps);
+  }
+
   // one accumulator set per 64-k group of the warp: independent MMA chains
   float acc[2][GPW][NT][4];
 #pragma unroll
@@ -261,8 +298,9 @@ __global__ void __launch_bounds__(gv_threads(QW), gv_min_ctas(NT)) qmm_gemv_kern
         for (int d = 0; d < 2; ++d)
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
-            xr[bb][d][nt] = xon[nt] ? lds128(stg + xbase + bb * L::kXBox + nt * 1024 + xch[d])
-                                    : make_uint4(0u, 0u, 0u, 0u);
+            xr[bb][d][nt] = !xon[nt] ? make_uint4(0u, 0u, 0u, 0u)
+                            : norm   ? lds128(nx + i * 4 * nxbox + nxrow + bb * nxbox + xch[d])
+                                     : lds128(stg + xbase + bb * L::kXBox + nt * 1024 + xch[d]);
       uint2 cw[2][2][GPW];
       uint32_t sb[2][2][GPW];
 #pragma unroll
@@ -470,13 +508,15 @@ __global__ void __launch_bounds__(gv_threads(QW), gv_min_ctas(NT)) qmm_gemv_kern
 }
 
 int g_gv_sms = 0;
+// shared memory a launch may add for the rows of a fused RMSNorm
+constexpr int kGvNormSmem = 24 * 1024;
 bool g_gv_attr[2][2] = {{false, false}, {false, false}};
 
 template <int NT, int QW>
 int gv_set_attr() {
   if (!g_gv_attr[NT - 1][QW / 4]) {
     IAM_CUDA(cudaFuncSetAttribute(qmm_gemv_kernel<NT, QW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  GvLayout<NT, QW>::kSmem));
+                                  GvLayout<NT, QW>::kSmem + kGvNormSmem));
     g_gv_attr[NT - 1][QW / 4] = true;
   }
   return IAM_OK;
@@ -505,10 +545,17 @@ template <int NT, int QW>
 int gv_launch(const QmmGvArgs& ga, int ks, cudaStream_t st, bool pdl) {
   const int r = gv_set_attr<NT, QW>();
   if (r != IAM_OK) return r;
+  // fused RMSNorm: the CTA's input rows, 4 boxes of M rows x 128 bytes a block
+  size_t extra = 0;
+  if (ga.a.norm_w) {
+    const int nkb = (qp_kblocks(ga.a.K) + ks - 1) / ks;
+    extra = 16 + static_cast<size_t>(nkb) * 4 * ga.a.M * 128;
+    IAM_CHECK(extra <= static_cast<size_t>(kGvNormSmem), "qmm: the fused RMSNorm's rows do not fit");
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ga.a.total_ctas, 1, ks);
   cfg.blockDim = dim3(gv_threads(QW), 1, 1);
-  cfg.dynamicSmemBytes = GvLayout<NT, QW>::kSmem;
+  cfg.dynamicSmemBytes = GvLayout<NT, QW>::kSmem + extra;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

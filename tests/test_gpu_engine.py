@@ -177,6 +177,29 @@ def test_device_resident_step_on_fresh_weights(K):
     check_argmax(got[0][0], logits)
 
 
+@pytest.mark.parametrize("K", [1, 2])
+def test_fused_rmsnorm_bit_identical(K, monkeypatch):
+    """Steps of at most two rows fuse the RMSNorm ahead of each matmul into
+    the matmul (its CTAs normalise the rows they read); the outputs must be
+    bit-identical to the separate norm kernel's (IAM_FUSED_NORM=0)."""
+    d = O.TINY
+    tokens = SM.draft_tokens(SEED, d, K, tag=f"fn{K}")
+    got = []
+    for fused in ("1", "0"):
+        monkeypatch.setenv("IAM_FUSED_NORM", fused)
+        e = I.Engine(cdims(d, 64, 8))
+        e.init_synthetic(SEED)
+        e.state_init(SEED, 20)
+        am, acc = e.verify(tokens, 20)
+        am2, _ = e.verify(tokens[:1], 20 + K)
+        got.append((list(am), acc, e.read_hidden(1).copy(), list(am2)))
+        prof = e.profile_step(K, 20 + K + 1)
+        assert ("rmsnorm" in prof and prof["rmsnorm"]["launches"] == (1 if fused == "1" else 2 * d.n_layers + 1)), prof
+        e.close()
+    assert got[0][0] == got[1][0] and got[0][1] == got[1][1] and got[0][3] == got[1][3]
+    assert np.array_equal(got[0][2], got[1][2])
+
+
 def test_tiny_model_verify_wide_block():
     """K = 48: every matmul of the step (fused projections, SwiGLU, residual,
     lm_head argmax) on the tensor-core kernel's 64-token tile."""
