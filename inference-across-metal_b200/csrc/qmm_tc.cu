@@ -302,8 +302,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     Ring<XS> xr;
     for (int i = 0; i < nkb; ++i, ar.next(), xr.next()) {
       const int slot = ar.idx, xsl = xr.idx;
-      named_bar_sync(3, 64);  // with the watcher: block i is ready, or the CTA gave up
-      if (*abort_flag) {
+      // with the watcher: block i is ready, or (the OR of the barrier) the CTA
+      // gave up -- no shared-memory read on this path
+      if (named_bar_or(3, 64, false)) {
         ok = false;
         break;
       }
@@ -334,7 +335,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     for (int i = 0; i < nkb; ++i, ar.next()) {
       const bool got = __all_sync(0xffffffffu, !*abort_flag && mbar_wait_light(afull(ar.idx), ar.phase, abort_flag, lim));
       if (!got && lane == 0) give_up();
-      named_bar_sync(3, 64);
+      named_bar_or(3, 64, !got);
       if (!got) break;
     }
   } else {
