@@ -159,7 +159,7 @@ __device__ __forceinline__ void store_state(const float (&S)[RPW][4], float* Sh,
 // gated norm's sum of squares over dv is exchanged through distributed
 // shared memory (summed in rank order).  C = 1 is the one-CTA-a-head kernel.
 // kSeq: one launch over several sequences, grid.y = sequence (GdnArgs n_seq).
-template <int C, bool kSeq>
+template <int C, bool kSeq, bool kSpread>
 __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a) {
   constexpr int R = kHD / C, RPW = R / (kThreads / 32);
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
   // fetched before the grid-dependency wait); shorter blocks spread the
   // (token, channel) pairs over all threads.  Measured on the 27B step: the
   // first is 0.17 ms faster at K = 32, the second 0.08 ms faster at K = 1.
-  const bool seq_conv = a.rows >= kConvSeqRows;
+  constexpr bool seq_conv = !kSpread;  // one kernel a schedule (each allocates its own registers)
   const int ct = threadIdx.x;
   const int my_col = ct < nch ? chan_col(ct) : -1;
   float k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fused_kernel(const GdnArgs a)
       sm.g[t] = gv;
       sm.beta[t] = bv;
     }
-#pragma unroll 4
+#pragma unroll 2
     for (int idx = threadIdx.x; !seq_conv && idx < n * nch; idx += kThreads) {
       const int t = idx / nch, ci = idx - t * nch;
       const int col = chan_col(ci);
@@ -411,9 +411,14 @@ int ensure_attrs() { return gdn_init_attrs(); }
 
 int gdn_init_attrs() {
   if (g_attr_done) return IAM_OK;
-  for (auto* k : {gdn_fused_kernel<1, false>, gdn_fused_kernel<2, false>, gdn_fused_kernel<4, false>,
-                  gdn_fused_kernel<8, false>, gdn_fused_kernel<1, true>, gdn_fused_kernel<2, true>,
-                  gdn_fused_kernel<4, true>, gdn_fused_kernel<8, true>})
+  for (auto* k : {gdn_fused_kernel<1, false, false>, gdn_fused_kernel<2, false, false>,
+                  gdn_fused_kernel<4, false, false>, gdn_fused_kernel<8, false, false>,
+                  gdn_fused_kernel<1, true, false>, gdn_fused_kernel<2, true, false>,
+                  gdn_fused_kernel<4, true, false>, gdn_fused_kernel<8, true, false>,
+                  gdn_fused_kernel<1, false, true>, gdn_fused_kernel<2, false, true>,
+                  gdn_fused_kernel<4, false, true>, gdn_fused_kernel<8, false, true>,
+                  gdn_fused_kernel<1, true, true>, gdn_fused_kernel<2, true, true>,
+                  gdn_fused_kernel<4, true, true>, gdn_fused_kernel<8, true, true>})
     IAM_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(GdnSmem)));
   int dev = 0;
   IAM_CUDA(cudaGetDevice(&dev));
@@ -446,7 +451,11 @@ int launch_gdn_c(const GdnArgs& a, cudaStream_t st, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  IAM_CUDA(cudaLaunchKernelEx(&cfg, gdn_fused_kernel<C, kSeq>, a));
+  if (a.rows >= kConvSeqRows) {
+    IAM_CUDA(cudaLaunchKernelEx(&cfg, gdn_fused_kernel<C, kSeq, false>, a));
+  } else {
+    IAM_CUDA(cudaLaunchKernelEx(&cfg, gdn_fused_kernel<C, kSeq, true>, a));
+  }
   return IAM_OK;
 }
 

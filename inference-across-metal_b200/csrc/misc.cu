@@ -248,6 +248,22 @@ __device__ __forceinline__ unsigned long long best_key_of_row(const unsigned lon
   return best;
 }
 
+// The best key of row r over the parts, by one warp (lane 0's result; the
+// maximum does not depend on the order).
+__device__ __forceinline__ unsigned long long best_key_of_row_warp(const unsigned long long* __restrict__ keys,
+                                                                  int nparts, int key_ld, int r, int lane) {
+  unsigned long long best = 0ull;
+  for (int i = lane; i < nparts; i += 32) {
+    const unsigned long long k = keys[static_cast<size_t>(i) * key_ld + r];
+    best = k > best ? k : best;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+    best = v > best ? v : best;
+  }
+  return best;
+}
+
 // Verify-block finalisation: reduce the lm_head's per-CTA keys of every row,
 // then the greedy accept length (largest j with tokens[j+1] == argmax[j] for
 // every smaller j; tokens[0] is the token being decoded).
@@ -257,10 +273,11 @@ __global__ void __launch_bounds__(1024) finalize_kernel(const unsigned long long
   pdl_wait();
   pdl_trigger();
   __shared__ int32_t am[kMaxRowsFinalize];
-  __shared__ unsigned long long sh[32];
-  for (int r = 0; r < M; ++r) {
-    const unsigned long long best = best_key_of_row(keys, nparts, key_ld, r, sh);
-    if (threadIdx.x == 0) {
+  // one warp a row, the rows in parallel
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < M; r += blockDim.x >> 5) {
+    const unsigned long long best = best_key_of_row_warp(keys, nparts, key_ld, r, lane);
+    if (lane == 0) {
       am[r] = static_cast<int32_t>(argmax_key_index(best));
       argmax_out[r] = am[r];
     }
@@ -277,10 +294,10 @@ __global__ void __launch_bounds__(1024) best_keys_kernel(const unsigned long lon
                                                          int key_ld, int M, unsigned long long* best_out) {
   pdl_wait();
   pdl_trigger();
-  __shared__ unsigned long long sh[32];
-  for (int r = 0; r < M; ++r) {
-    const unsigned long long best = best_key_of_row(keys, nparts, key_ld, r, sh);
-    if (threadIdx.x == 0) best_out[r] = best;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < M; r += blockDim.x >> 5) {
+    const unsigned long long best = best_key_of_row_warp(keys, nparts, key_ld, r, lane);
+    if (lane == 0) best_out[r] = best;
   }
 }
 

@@ -213,6 +213,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     for (int i = 0; i < kQmmMaxSeg; ++i)  // constant indices: constant-bank loads
       if (i == si) *seg_copy = A.seg[i];
     fence_mbar_init();
+    // the first weight blocks go out now, before the tensor-memory allocation
+    // and the CTA barrier (this thread is also the producer below)
+    if (!A.starve) {
+      const unsigned char* wsrc = seg_copy->packed + (static_cast<size_t>(tile) * KB + kb0) * kQpBlockBytes;
+      for (int i = 0; i < min(nkb, WS); ++i) {
+        mbar_expect_tx(wfull(i), kQpBlockBytes);
+        bulk_load(sbase + L::kWOff + i * kQpBlockBytes, wsrc + static_cast<size_t>(i) * kQpBlockBytes, kQpBlockBytes,
+                  wfull(i));
+      }
+    }
   }
   if (warp == 0) {
     __syncwarp();
@@ -254,9 +264,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
       };
       // (a starved launch, a test's fault injection, issues nothing: the
       // consumers' first waits can only run out)
+      // (the first min(nkb, WS) weight blocks went out at the start: weights
+      // do not depend on the preceding kernel)
       int iw = A.starve ? 0 : min(nkb, WS), ix = A.starve ? 0 : min(nkb, XS);
-      // weights do not depend on the preceding kernel: start them first
-      for (int i = 0; i < iw; ++i) load_w(i);
       pdl_wait();
       for (int i = 0; i < ix; ++i) load_x(i);
       uint32_t idle = 0;
