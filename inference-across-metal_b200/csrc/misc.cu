@@ -47,11 +47,62 @@ __global__ void __launch_bounds__(512) rms_norm_kernel(const uint16_t* __restric
   }
 }
 
+// The same for rows of exactly 256 * NJ elements, small enough (256
+// threads, 1 KiB of shared memory, the row in registers) to become resident
+// next to a matmul CTA that holds most of an SM, so that under programmatic
+// dependent launch it starts early and runs the moment its input is written:
+// thread t is the reference's thread t (it sums x[t + 256 j]^2 in j order) and
+// the reference's tree (partial[t] += partial[t + s], s = 128 .. 1) runs
+// through shared memory for s >= 32 and lane shuffles below.
+template <int NJ>
+__global__ void __launch_bounds__(256) rms_norm_row_kernel(const uint16_t* __restrict__ x, int ldx,
+                                                           const uint16_t* __restrict__ w,
+                                                           uint16_t* __restrict__ out, int ldo, float eps) {
+  __shared__ float part[256];
+  const int row = blockIdx.x, t = threadIdx.x;
+  uint16_t wv[NJ], xv[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) wv[j] = w[t + 256 * j];  // before the wait: weights only
+  pdl_wait();
+  pdl_trigger();
+  const uint16_t* xr = x + static_cast<size_t>(row) * ldx;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) xv[j] = xr[t + 256 * j];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const float v = bf2f(xv[j]);
+    sum += v * v;
+  }
+  part[t] = sum;
+  __syncthreads();
+  if (t < 128) part[t] += part[t + 128];
+  __syncthreads();
+  if (t < 64) part[t] += part[t + 64];
+  __syncthreads();
+  if (t < 32) {
+    float v = part[t] + part[t + 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_down_sync(0xffffffffu, v, o);
+      if (t < o) v += u;
+    }
+    if (t == 0) part[0] = sqrtf(v / static_cast<float>(256 * NJ) + eps);
+  }
+  __syncthreads();
+  const float rms = part[0];
+  uint16_t* orow = out + static_cast<size_t>(row) * ldo;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) orow[t + 256 * j] = f2bf((bf2f(xv[j]) / rms) * bf2f(wv[j]));
+}
+
 int launch_rms_norm(const uint16_t* x, int ldx, const uint16_t* w, uint16_t* out, int ldo, int rows, int dim,
                     float eps, cudaStream_t st, bool pdl) {
   IAM_CHECK(dim % 256 == 0 && dim <= 16384, "rms_norm: dim must be a multiple of 256, at most 16384");
   IAM_CHECK(aligned16(x) && aligned16(w) && aligned16(out) && ldx % 8 == 0 && ldo % 8 == 0,
             "rms_norm: 16-byte aligned rows required");
+  if (dim == 5120)  // the 27B hidden size
+    return launch_k(rms_norm_row_kernel<20>, dim3(rows), dim3(256), 0, st, pdl, x, ldx, w, out, ldo, eps);
   return launch_k(rms_norm_kernel, dim3(rows), dim3(std::min(512, std::max(32, dim / 8))),
                   static_cast<size_t>(dim) * 2, st, pdl, x, ldx, w, out, ldo, dim, eps);
 }

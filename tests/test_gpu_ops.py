@@ -74,6 +74,24 @@ def test_rms_norm_golden(golden):
     assert np.array_equal(host_u16(out), golden["rms_norm.out"])
 
 
+@pytest.mark.parametrize("rows,dim", [(33, 5120), (9, 2560), (4, 256)])
+def test_rms_norm_rows(rows, dim):
+    """Both schedules (the register-resident one for the 5120-wide hidden state
+    and the shared-memory one for other widths) against the oracle: every
+    element within one bf16 step, nearly all of them identical."""
+    rng = np.random.default_rng(rows * 7 + dim)
+    xh = O.to_u16(rng.standard_normal((rows, dim)).astype(np.float32) * 3)
+    wh = O.to_u16(1 + 0.1 * rng.standard_normal(dim).astype(np.float32))
+    x, w = dev(xh, torch), dev(wh, torch)
+    out = empty_u16(torch, rows, dim)
+    I.rms_norm_bf16(ptr(x), ptr(w), ptr(out), rows, dim, 1e-6)
+    sync()
+    got = host_u16(out).astype(np.int32)
+    ref = O.to_u16(O.rms_norm(O.from_u16(xh), O.from_u16(wh))).astype(np.int32)
+    diff = np.abs(got - ref)
+    assert diff.max() <= 1 and (diff == 0).mean() > 0.99
+
+
 def test_elementwise_golden(golden):
     a, b = dev(golden["ew.a"], torch), dev(golden["ew.b"], torch)
     n = golden["ew.a"].size
