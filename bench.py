@@ -418,6 +418,73 @@ def profile_step(args):
     e.close()
 
 
+MATRIX_OF_GRID_X = {40: "out_proj|o_proj|down", 272: "gate_up", 130: "in_proj", 112: "q|k|v", 1940: "lm_head"}
+
+
+def trace_step(args):
+    """The kernels of graph steps as they run, with programmatic overlap:
+    CUPTI's activity records (through torch.profiler) of three replays of the
+    64-layer step at verify width --k, after warm-up.  Per kernel kind (and
+    per matrix for the matmuls): launches, mean duration, and the exposed
+    time -- how far each launch extends the step past the end of the
+    launches before it, which sums to the step.  One JSON line per kind;
+    the trace file goes to --trace-out."""
+    import numpy as np
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    import iam_b200 as I
+    K = args.k
+    d = I.Dims.qwen35_27b(max_ctx=CTX + 256, max_rows=max(K, 32))
+    e = I.Engine(d)
+    e.init_synthetic(SEED)
+    e.state_init(SEED, CTX)
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    toks = torch.from_numpy(np.random.default_rng(0).integers(0, d.vocab, K).astype(np.int32)).cuda()
+    for _ in range(20):
+        e.verify_device(toks.data_ptr(), K, CTX, None, st.cuda_stream)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(10):
+        e.verify_device(toks.data_ptr(), K, CTX, None, st.cuda_stream)
+    b.record(st)
+    torch.cuda.synchronize()
+    untraced = a.elapsed_time(b) / 10
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(3):
+            e.verify_device(toks.data_ptr(), K, CTX, None, st.cuda_stream)
+        torch.cuda.synchronize()
+    prof.export_chrome_trace(args.trace_out)
+    e.close()
+    with open(args.trace_out) as f:
+        ev = [x for x in json.load(f)["traceEvents"] if x.get("cat") == "kernel"]
+    ev.sort(key=lambda x: x["ts"])
+    n = len(ev) // 3
+    ev = ev[n:2 * n]  # the middle replay
+    kinds = {}
+    prev_end = ev[0]["ts"]
+    for x in ev:
+        s, dur = x["ts"], x["dur"]
+        exposed = max(0.0, s + dur - max(s, prev_end))
+        prev_end = max(prev_end, s + dur)
+        name = x["name"]
+        kind = next((k for k in ("qmm_gemv", "qmm_tc", "rms_norm", "gdn_fused", "attn_prep", "attn_decode_tc",
+                                  "attn_decode", "attn_combine", "finalize", "embed", "advance") if k in name),
+                    name[:40])
+        if kind.startswith("qmm"):
+            kind += " " + MATRIX_OF_GRID_X.get(x["args"].get("grid", [0])[0], str(x["args"].get("grid")))
+        r = kinds.setdefault(kind, [0, 0.0, 0.0])
+        r[0] += 1
+        r[1] += dur
+        r[2] += exposed
+    span = prev_end - ev[0]["ts"]
+    print(json.dumps({"trace_step": K, "launches": n, "span_us": round(span, 1), "untraced_ms": round(untraced, 3)}))
+    for kind, (cnt, tot, expo) in sorted(kinds.items(), key=lambda kv: -kv[1][2]):
+        print(json.dumps({"kind": kind, "launches": cnt, "mean_us": round(tot / cnt, 2),
+                          "exposed_us": round(expo, 1), "exposed_share": round(expo / span, 4)}))
+
+
 def profile_small(args):
     """Two graph steps of a 4-layer full-width model (3 GDN + 1 attention
     layer, vocab 32768, context 1024: about 2.5 GB on the device) at verify
@@ -706,6 +773,8 @@ def main():
     ap.add_argument("--impl", default="iam")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--profile-step", action="store_true", help="two graph steps at --k, for ncu launch lists")
+    ap.add_argument("--trace-step", action="store_true", help="in-graph kernel timeline of the step at --k (CUPTI)")
+    ap.add_argument("--trace-out", default="gpurun_out/trace_step.json", help="chrome trace file of --trace-step")
     ap.add_argument("--profile-small", action="store_true",
                     help="two graph steps of a 4-layer full-width model at --k, for per-kernel ncu captures")
     ap.add_argument("--profile-qmm", default=None,
@@ -724,6 +793,8 @@ def main():
         return qmm_sweep(args)
     if args.profile_step:
         return profile_step(args)
+    if args.trace_step:
+        return trace_step(args)
     if args.profile_small:
         return profile_small(args)
     if args.profile_qmm:
