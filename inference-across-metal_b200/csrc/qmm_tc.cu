@@ -51,6 +51,7 @@ namespace {
 // every 256-k block.
 constexpr int kTcDqWarps = 16;
 constexpr int kTcThreads = 32 * (3 + kTcDqWarps);  // + a watcher warp (the last)
+constexpr int kTcEarly = 2;                           // weight blocks issued before the CTA barrier
 constexpr int kTcASlots = 3;                         // TMEM A slots of one 256-k block (128 columns)
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcDCol = 128 * kTcASlots;        // accumulator: NN (<= 64) columns
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
     // and the CTA barrier (this thread is also the producer below)
     if (!A.starve) {
       const unsigned char* wsrc = seg_copy->packed + (static_cast<size_t>(tile) * KB + kb0) * kQpBlockBytes;
-      for (int i = 0; i < min(nkb, WS); ++i) {
+      for (int i = 0; i < min(nkb, kTcEarly); ++i) {
         mbar_expect_tx(wfull(i), kQpBlockBytes);
         bulk_load(sbase + L::kWOff + i * kQpBlockBytes, wsrc + static_cast<size_t>(i) * kQpBlockBytes, kQpBlockBytes,
                   wfull(i));
@@ -266,7 +267,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) qmm_tc_kernel(const __grid_cons
       // consumers' first waits can only run out)
       // (the first min(nkb, WS) weight blocks went out at the start: weights
       // do not depend on the preceding kernel)
-      int iw = A.starve ? 0 : min(nkb, WS), ix = A.starve ? 0 : min(nkb, XS);
+      int iw = A.starve ? 0 : min(nkb, kTcEarly), ix = A.starve ? 0 : min(nkb, XS);
+      // the rest of the ring's first lap: behind the first blocks, so those
+      // arrive first when every CTA of the launch starts at once
+      if (!A.starve)
+        for (; iw < min(nkb, WS); ++iw) load_w(iw);
       pdl_wait();
       for (int i = 0; i < ix; ++i) load_x(i);
       uint32_t idle = 0;
