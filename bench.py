@@ -421,13 +421,42 @@ def profile_step(args):
 MATRIX_OF_GRID_X = {40: "out_proj|o_proj|down", 272: "gate_up", 130: "in_proj", 112: "q|k|v", 1940: "lm_head"}
 
 
+def kernel_kind(name: str, grid) -> str:
+    """The kind a kernel record is summed under (per matrix for the matmuls)."""
+    kind = next((k for k in ("qmm_gemv", "qmm_tc", "rms_norm", "gdn_fused", "attn_prep", "attn_decode_tc",
+                              "attn_decode", "attn_combine", "finalize", "embed", "advance") if k in name), name[:40])
+    if kind.startswith("qmm"):
+        kind += " " + MATRIX_OF_GRID_X.get((grid or [0])[0], str(grid))
+    return kind
+
+
+def exposed_by_kind(events):
+    """Kernel records (ts, dur in us; name; args.grid), sorted by start, of one
+    step: per kind [launches, summed duration, exposed time], and the step's
+    span.  A launch's exposed time is how far it extends the span past the
+    end of every launch before it, so however the launches overlap the
+    exposed times sum to the span less the gaps in which no kernel runs."""
+    kinds = {}
+    t0 = prev_end = events[0]["ts"]
+    for x in events:
+        s, dur = x["ts"], x["dur"]
+        exposed = max(0.0, s + dur - max(s, prev_end))
+        prev_end = max(prev_end, s + dur)
+        r = kinds.setdefault(kernel_kind(x["name"], x.get("args", {}).get("grid")), [0, 0.0, 0.0])
+        r[0] += 1
+        r[1] += dur
+        r[2] += exposed
+    return kinds, prev_end - t0
+
+
 def trace_step(args):
     """The kernels of graph steps as they run, with programmatic overlap:
     CUPTI's activity records (through torch.profiler) of three replays of the
     64-layer step at verify width --k, after warm-up.  Per kernel kind (and
     per matrix for the matmuls): launches, mean duration, and the exposed
     time -- how far each launch extends the step past the end of the
-    launches before it, which sums to the step.  One JSON line per kind;
+    launches before it (the sum is the step less its idle gaps).  One JSON
+    line per kind;
     the trace file goes to --trace-out."""
     import numpy as np
     import torch
@@ -461,24 +490,7 @@ def trace_step(args):
         ev = [x for x in json.load(f)["traceEvents"] if x.get("cat") == "kernel"]
     ev.sort(key=lambda x: x["ts"])
     n = len(ev) // 3
-    ev = ev[n:2 * n]  # the middle replay
-    kinds = {}
-    prev_end = ev[0]["ts"]
-    for x in ev:
-        s, dur = x["ts"], x["dur"]
-        exposed = max(0.0, s + dur - max(s, prev_end))
-        prev_end = max(prev_end, s + dur)
-        name = x["name"]
-        kind = next((k for k in ("qmm_gemv", "qmm_tc", "rms_norm", "gdn_fused", "attn_prep", "attn_decode_tc",
-                                  "attn_decode", "attn_combine", "finalize", "embed", "advance") if k in name),
-                    name[:40])
-        if kind.startswith("qmm"):
-            kind += " " + MATRIX_OF_GRID_X.get(x["args"].get("grid", [0])[0], str(x["args"].get("grid")))
-        r = kinds.setdefault(kind, [0, 0.0, 0.0])
-        r[0] += 1
-        r[1] += dur
-        r[2] += exposed
-    span = prev_end - ev[0]["ts"]
+    kinds, span = exposed_by_kind(ev[n:2 * n])  # the middle replay
     print(json.dumps({"trace_step": K, "launches": n, "span_us": round(span, 1), "untraced_ms": round(untraced, 3)}))
     for kind, (cnt, tot, expo) in sorted(kinds.items(), key=lambda kv: -kv[1][2]):
         print(json.dumps({"kind": kind, "launches": cnt, "mean_us": round(tot / cnt, 2),
